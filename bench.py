@@ -1,0 +1,364 @@
+"""Benchmark of the MXFP4 hot path on B200 (contract: one JSON line on rank 0).
+
+Headline workload ("training activation quantize"):
+BF16 [16384, 8192], N(0,1) x per-row 10^U(-2,2), seed 1, quantized rowwise AND
+columnwise to MXFP4 in one pass by mxb_quant_mxfp4_rowcol.  A step is one such
+pass; `value` is algorithmic HBM GB/s (bytes that must be read + written once:
+411,041,792 per step) with the input resident in HBM; `e2e` is the same
+metric through the C ABI with pinned host buffers, host<->device copies
+inside the timed region.  Other ops of the path are timed the same way and
+reported under "ops" (device-resident, GB/s and fraction of measured HBM).
+
+--gpus N (torchrun, one process per GPU): every rank quantizes its own
+[16384, 8192] shard (row sharding, weak scaling, no collective in the data
+path); value = total bytes of all ranks / max-over-ranks time.
+
+--impl reference: the reference has no CPU implementation of this path, and
+its CUDA kernels are not a CPU path either, so the reference arm times the
+bit-exact C restatement of the reference kernels (oracle/, "port") on all host
+cores, on the same workload, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "mxfp4-hopper_b200"))
+
+M2, K2 = 16384, 8192
+ALG_BYTES_ROWCOL = M2 * K2 * 2 + 2 * (M2 * K2 // 2 + M2 * K2 // 32)  # 411,041,792
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the headline
+# kernel from one ncu capture (profiles/quant_rowcol_config2.md); None until measured.
+NCU_TRAFFIC_ROWCOL = None
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True,
+                                     text=True, timeout=5).stdout.strip()
+                if out:
+                    self.rows.append([c.strip() for c in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        import statistics
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), \
+        int(os.environ.get("LOCAL_RANK", 0))
+
+
+# --------------------------------------------------------------------------- CPU arm
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    from mxfp4_b200 import synthetic as syn
+    from oracle import oracle as O
+
+    O.build()
+    cores = os.cpu_count() or 1
+    O.set_threads(cores)
+    xb = syn.bf16_bits(syn.config2())
+    for _ in range(max(args.warmup, 0)):
+        O.quant_rows(xb)
+        O.quant_cols(xb)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.quant_rows(xb)
+        O.quant_cols(xb)
+    dt = (time.perf_counter() - t0) / args.steps
+    gbs = ALG_BYTES_ROWCOL / dt / 1e9
+    line = {
+        "metric": "mxfp4_quant_rowcol_hbm_gbs", "value": round(gbs, 3), "unit": "GB/s",
+        "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16->mxfp4 (u8)", "data": "synthetic",
+        "config": {"workload": "config2 rowwise+columnwise MXFP4 quantize [16384,8192] bf16",
+                   "rows": M2, "cols": K2, "seed": 1},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": "full config-2 tensor per step (oracle/mxfp4_oracle.c, "
+                                   "OpenMP rows+cols quantize)"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def cpu_baseline_sample():
+    """Oracle (port) on the host cores: config-2 rows+cols quantize, ~10 s budget."""
+    from mxfp4_b200 import synthetic as syn
+    from oracle import oracle as O
+
+    O.build()
+    cores = os.cpu_count() or 1
+    O.set_threads(cores)
+    rows = 4096
+    xb = syn.bf16_bits(syn.config2(rows, K2))
+    O.quant_rows(xb)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.quant_rows(xb)
+        O.quant_cols(xb)
+        n += 1
+        if time.perf_counter() - t0 > 8.0 or n >= 50:
+            break
+    dt = (time.perf_counter() - t0) / n
+    alg = rows * K2 * 2 + 2 * (rows * K2 // 2 + rows * K2 // 32)
+    return {"value": round(alg / dt / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"config-2 rows 0..{rows} (1/4 of the tensor), {n} reps, oracle rows+cols"}
+
+
+# --------------------------------------------------------------------------- GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ops", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from mxfp4_b200 import capi
+    from mxfp4_b200 import synthetic as syn
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    capi.load()
+    peak, peak_kind = measured_peaks()
+    warm = max(args.warmup, 3)
+
+    x = syn.config2().to(dev)
+    cr = torch.empty(M2, K2 // 2, dtype=torch.uint8, device=dev)
+    sr = torch.empty(M2, K2 // 32, dtype=torch.uint8, device=dev)
+    cc = torch.empty(K2, M2 // 2, dtype=torch.uint8, device=dev)
+    sc = torch.empty(K2, M2 // 32, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def step():
+        capi.call("mxb_quant_mxfp4_rowcol", x.data_ptr(), M2, K2, K2, cr.data_ptr(), sr.data_ptr(),
+                  cc.data_ptr(), sc.data_ptr(), None, 1e-10, -6.0, 6.0, sh)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(warm):
+        step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms = max_over_ranks(ms)
+    value = ALG_BYTES_ROWCOL * world / (ms * 1e-3) / 1e9
+    kernel_gbs = ALG_BYTES_ROWCOL / (ms * 1e-3) / 1e9
+
+    # ---- end to end through the C ABI: pinned host input -> device -> pinned host outputs
+    xh = x.cpu().pin_memory()
+    outs_h = [torch.empty_like(t, device="cpu").pin_memory() for t in (cr, sr, cc, sc)]
+    h2d = xh.numel() * 2
+    d2h = sum(t.numel() for t in outs_h)
+
+    def e2e_step():
+        x.copy_(xh, non_blocking=True)
+        step()
+        for h, d in zip(outs_h, (cr, sr, cc, sc)):
+            h.copy_(d, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e2e_steps = max(3, min(args.steps, 10))
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    e2e_val = ALG_BYTES_ROWCOL * world / (e2e_ms * 1e-3) / 1e9
+    del xh, outs_h
+
+    ops = {} if args.no_ops else time_other_ops(dev, stream, peak)
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
+    cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline_sample()
+    line = {
+        "metric": "mxfp4_quant_rowcol_hbm_gbs", "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": warm, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16->mxfp4 (u8)", "data": "synthetic (seeded N(0,1) x per-row 10^U(-2,2))",
+        "config": {"workload": "config2 rowwise+columnwise MXFP4 quantize [16384,8192] bf16 per GPU",
+                   "rows_per_gpu": M2, "cols": K2, "parallelism": f"row-shard x{world}",
+                   "l2": "inputs (268 MB) larger than L2 (126 MB)"},
+        "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 2), "peak": peak,
+                     "unit": "GB/s", "frac": round(kernel_gbs / peak, 4),
+                     "peak_source": peak_kind,
+                     "traffic": NCU_TRAFFIC_ROWCOL,
+                     "alg_bytes_per_launch": ALG_BYTES_ROWCOL,
+                     "kernel": "quant_rowcol_kernel<true,true>"},
+        "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+        "ops": ops,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def time_other_ops(dev, stream, peak):
+    """Device-resident GB/s of the other kernels of the path on their BASELINE shapes."""
+    import torch
+
+    from mxfp4_b200 import capi
+    from mxfp4_b200 import synthetic as syn
+
+    sh = stream.cuda_stream
+    res = {}
+
+    def timeit(fn, alg_bytes, n=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = a.elapsed_time(b) / n
+        gbs = alg_bytes / (ms * 1e-3) / 1e9
+        return {"us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+
+    # Q-row alone on config 2
+    x = syn.config2().to(dev)
+    q = torch.empty(M2, K2 // 2, dtype=torch.uint8, device=dev)
+    s = torch.empty(M2, K2 // 32, dtype=torch.uint8, device=dev)
+    res["quant_rows_config2"] = timeit(
+        lambda: capi.call("mxb_per_token_group_quant_fp4", x.data_ptr(), M2, K2, K2, q.data_ptr(),
+                          s.data_ptr(), 32, 1e-10, -6.0, 6.0, 0, sh),
+        M2 * K2 * 2 + M2 * K2 // 2 + M2 * K2 // 32)
+    del x, q, s
+    # config 3: codes [16384, 8192] u8 (K = 16384 elements), scales [16384, 512]
+    c, sc = (t.to(dev) for t in syn.config3())
+    M3, Kb3 = c.shape
+    out = torch.empty(M3, 2 * Kb3, dtype=torch.bfloat16, device=dev)
+    res["dequant_bf16_config3"] = timeit(
+        lambda: capi.call("mxb_per_token_Mxfp4ToBf16_dequant", c.data_ptr(), sc.data_ptr(), M3, Kb3,
+                          out.data_ptr(), sh), M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 4)
+    del out
+    f8 = torch.empty(M3, 2 * Kb3, dtype=torch.uint8, device=dev)
+    fs = torch.empty(Kb3 // 64, M3, dtype=torch.float32, device=dev)
+    res["mxfp4_to_fp8_rows_config3"] = timeit(
+        lambda: capi.call("mxb_per_token_Mxfp4ToFp8", c.data_ptr(), sc.data_ptr(), M3, Kb3,
+                          f8.data_ptr(), fs.data_ptr(), sh),
+        M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + (Kb3 // 64) * M3 * 4)
+    del fs
+    fcs = torch.empty(M3 // 128, 2 * Kb3, dtype=torch.float32, device=dev)
+    res["mxfp4_to_fp8_col_config3"] = timeit(
+        lambda: capi.call("mxb_per_token_Mxfp4ToFp8_col", c.data_ptr(), sc.data_ptr(), M3, Kb3,
+                          f8.data_ptr(), fcs.data_ptr(), sh),
+        M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fcs.numel() * 4)
+    res["mxfp4_to_fp8_colT_config3"] = timeit(
+        lambda: capi.call("mxb_per_token_Mxfp4RowToBf16ToFp8Col", c.data_ptr(), sc.data_ptr(), M3,
+                          2 * Kb3, f8.data_ptr(), fcs.data_ptr(), 1e-10, sh),
+        M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fcs.numel() * 4)
+    del c, sc, f8, fcs
+    # config 4 per-token FP8
+    x4 = syn.config4().to(dev)
+    M4, K4 = x4.shape
+    q4 = torch.empty(M4, K4, dtype=torch.uint8, device=dev)
+    s4 = torch.empty(M4, dtype=torch.float32, device=dev)
+    alg4 = M4 * K4 * 2 + M4 * K4 + M4 * 4
+    res["fp8_quant_config4"] = timeit(
+        lambda: capi.call("mxb_per_token_quant_fp8", x4.data_ptr(), M4, K4, q4.data_ptr(),
+                          s4.data_ptr(), 1e-10, sh), alg4)
+    res["fp8_dequant_config4"] = timeit(
+        lambda: capi.call("mxb_per_token_dequant_fp8", q4.data_ptr(), s4.data_ptr(), M4, K4,
+                          x4.data_ptr(), sh), alg4)
+    return res
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,164 @@
+/*
+ * mxfp4_b200.h -- C ABI of the B200 (sm_100a) MXFP4 quantize / dequantize /
+ * convert library (libmxfp4_b200.so).
+ *
+ * Every entry point takes raw device pointers, sizes in elements (or bytes
+ * where named `_bytes`), and a CUDA stream (`mxb_stream_t` is ABI-identical to
+ * `cudaStream_t`; pass 0 for the legacy default stream).  Calls are
+ * asynchronous on that stream, allocate nothing, keep no state between calls
+ * and are safe to issue from several host threads.  The caller allocates every
+ * output, as the reference's Python wrappers do (code/kernel/api/mxfp4.py:110,
+ * code/kernel/api/mxfp4_dequant.py:61).  A non-zero status means nothing was
+ * launched; `mxb_last_error()` returns a message for the calling thread.
+ *
+ * Layouts (identical to the reference's, so its Megatron / Transformer Engine
+ * / DeepEP consumers read our outputs unchanged):
+ *   MXFP4 codes   uint8 [rows, cols/2]; element 2i in the low nibble
+ *                 (code/kernel/per_token_quant_mxfp4.cu:256).
+ *   E8M0 scales   uint8 [rows, cols/32], row-major, unpadded
+ *                 (code/kernel/api/mxfp4.py:135,155-161); byte e = 2^(e-127).
+ *   BF16 / FP8    bf16 / float8_e4m3fn bit patterns, row-major.
+ *
+ * Each declaration names the reference entry point it replaces (file:line in
+ * anonymous-git-2026/MXFP4-Hopper).
+ */
+#ifndef MXFP4_B200_H_
+#define MXFP4_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* mxb_stream_t;
+
+typedef enum {
+  MXB_OK = 0,
+  MXB_ERR_INVALID_ARGUMENT = 1, /* shape, stride or parameter out of contract */
+  MXB_ERR_MISALIGNED = 2,       /* a pointer or row pitch breaks the vector alignment */
+  MXB_ERR_CUDA = 3,             /* the launch itself failed */
+  MXB_ERR_UNSUPPORTED = 4       /* a mode the reference rejects too */
+} mxb_status;
+
+/* Message of the last non-OK status returned on this host thread. */
+const char* mxb_last_error(void);
+/* Library version string. */
+const char* mxb_version(void);
+
+/* ------------------------------------------------------------ quantize */
+
+/* Rowwise BF16 -> MXFP4, 1x32 blocks, E8M0 shared scale, E2M1 codes RNE.
+ * Replaces omo_per_token_group_quant_fp4 (code/kernel/ops.cu:28,
+ * code/kernel/per_token_quant_mxfp4.cu:387-487; kernel :121-266).
+ * input bf16 [M, K] with row pitch ldx elements (ldx % 8 == 0, 16-byte
+ * aligned base), K % 32 == 0; output_q uint8 [M, K/2]; output_s uint8
+ * [M, K/32].  group_size must be 32 and scale_ue8m0 0 (the reference's only
+ * live configuration: api/mxfp4.py:167-172).  eps is the initial block amax,
+ * fp4_min/fp4_max the clamp (reference defaults 1e-10, -6, 6). */
+mxb_status mxb_per_token_group_quant_fp4(const void* input, int64_t M, int64_t K, int64_t ldx,
+                                         void* output_q, void* output_s, int group_size,
+                                         float eps, float fp4_min, float fp4_max,
+                                         int scale_ue8m0, mxb_stream_t stream);
+
+/* Rowwise AND columnwise BF16 -> MXFP4 in one pass over the input.
+ * Replaces the Transformer Engine quantize of the reference
+ * (code/transformer_engine-2.8.diff:1464-1466): rowwise = Q-row of input,
+ * columnwise = Q-row of input.T.contiguous(), without materialising the
+ * transpose.  input bf16 [M, K], M % 32 == 0, K % 32 == 0;
+ * codes_row [M, K/2], scales_row [M, K/32] (both may be NULL for a
+ * columnwise-only call); codes_col [K, M/2], scales_col [K, M/32];
+ * scales_row_swizzled (nullable) receives the row scales again in the
+ * 128x4-tile layout of tcgen05 block-scaled MMA, padded to
+ * [round_up(M,128), round_up(K/32,4)] with zero padding
+ * (code/transformer_engine-2.8.diff:752-786). */
+mxb_status mxb_quant_mxfp4_rowcol(const void* input, int64_t M, int64_t K, int64_t ldx,
+                                  void* codes_row, void* scales_row, void* codes_col,
+                                  void* scales_col, void* scales_row_swizzled, float eps,
+                                  float fp4_min, float fp4_max, mxb_stream_t stream);
+
+/* Rewrites row-major E8M0 scales [M, S] into the 128x4-tile swizzled layout
+ * [round_up(M,128), round_up(S,4)] (zero padding).  Shape rule from
+ * MXFP4Quantizer.get_scale_shape (code/transformer_engine-2.8.diff:752-786). */
+mxb_status mxb_swizzle_scales(const void* scales, int64_t M, int64_t S, void* out,
+                              mxb_stream_t stream);
+
+/* ------------------------------------------------------------ dequantize */
+
+/* MXFP4 -> BF16.  Replaces omo_per_token_Mxfp4ToBf16_dequant
+ * (code/kernel/ops.cu:30, per_token_Mxfp4ToBf16_dequant.cu:164-240; kernel
+ * :70-160).  input uint8 [M, Kb] (Kb % 16 == 0), input_s uint8 [M, Kb/16],
+ * output bf16 [M, 2*Kb].  The reference's output_s is never written
+ * (per_token_Mxfp4ToBf16_dequant.cu:122) and is not taken here. */
+mxb_status mxb_per_token_Mxfp4ToBf16_dequant(const void* input, const void* input_s, int64_t M,
+                                             int64_t Kb, void* output, mxb_stream_t stream);
+
+/* MXFP4 -> FP8 E4M3 rowwise, 1x128 groups with power-of-two FP32 scales
+ * derived from the group's largest E8M0 exponent.  Replaces
+ * omo_per_token_Mxfp4ToFp8 (code/kernel/api/mxfp4_dequant.py:1,167;
+ * per_token_Mxfp4ToFp8.cu:239-310; kernel :92-235).  input uint8 [M, Kb]
+ * (Kb % 64 == 0), input_s uint8 [M, Kb/16], output_q fp8 [M, 2*Kb],
+ * output_s float [Kb/64, M] (M-contiguous, Transformer Engine GEMM_READY). */
+mxb_status mxb_per_token_Mxfp4ToFp8(const void* input, const void* input_s, int64_t M, int64_t Kb,
+                                    void* output_q, void* output_s, mxb_stream_t stream);
+
+/* Same operation under the name the reference binds at code/kernel/ops.cu:32
+ * (omo_per_token_Mxfp4ToBf16ToFp8, whose source the reference does not ship). */
+mxb_status mxb_per_token_Mxfp4ToBf16ToFp8(const void* input, const void* input_s, int64_t M,
+                                          int64_t Kb, void* output_q, void* output_s,
+                                          mxb_stream_t stream);
+
+/* MXFP4 -> transposed FP8 E4M3 with a scale per (128-row block, 32-column
+ * block) from the largest E8M0 exponent.  Replaces omo_per_token_Mxfp4ToFp8_col
+ * (code/kernel/ops.cu:40, per_token_Mxfp4ToFp8_col.cu:305-384; kernel
+ * :110-301), quirks included (outputs carry no sign; see DESIGN).  input uint8
+ * [M, Kb], M % 128 == 0, Kb % 128 == 0; output_q fp8 [2*Kb, M]; output_s
+ * float [M/128, 2*Kb]. */
+mxb_status mxb_per_token_Mxfp4ToFp8_col(const void* input, const void* input_s, int64_t M,
+                                        int64_t Kb, void* output_q, void* output_s,
+                                        mxb_stream_t stream);
+
+/* MXFP4 (rowwise) -> FP8 E4M3 columnwise with a true-amax scale per
+ * (128-row block, column): the wgrad operand.  Replaces
+ * omo_per_token_Mxfp4RowToBf16ToFp8Col (code/kernel/ops.cu:36,
+ * per_token_Mxfp4RowToBf16ToFp8Col.cu:204-247; kernel :42-197), with the
+ * kernel's missing barrier restored.  input uint8 [M, N/2], N % 32 == 0;
+ * input_s uint8 [M, N/32]; output_q fp8 [N, M]; output_s float
+ * [ceil(M/128), N] holding amax/448. */
+mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col(const void* input, const void* input_s,
+                                                int64_t M, int64_t N, void* output_q,
+                                                void* output_s, float eps, mxb_stream_t stream);
+
+/* As above for a grouped GEMM: rows split into num_splits segments of
+ * m_splits[i] rows, each quantized with power-of-two scales into its own
+ * contiguous [N, m_i] block at split_offsets[i] * N of output_q; scales
+ * (1/scale) at rows scale_offsets[i] + b of output_s [sum ceil(m_i/128), N].
+ * m_splits / split_offsets / scale_offsets are int32 DEVICE arrays; max_split_len
+ * bounds m_splits.  Replaces omo_per_token_Mxfp4RowToBf16ToFp8Col_msplit
+ * (code/kernel/ops.cu:38, per_token_Mxfp4RowToBf16ToFp8Col_msplit.cu:232-282;
+ * kernel :51-224). */
+mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit(
+    const void* input, const void* input_s, int64_t total_M, int64_t N, void* output_q,
+    void* output_s, const int32_t* m_splits, const int32_t* split_offsets,
+    const int32_t* scale_offsets, int64_t num_splits, int64_t max_split_len, float eps,
+    mxb_stream_t stream);
+
+/* ------------------------------------------------------------ per-token FP8 */
+
+/* BF16 -> FP8 E4M3 with one FP32 scale per row: amax = max(eps, max|x|),
+ * scale = amax/448, q = E4M3(clamp(x * 448/amax, +-448)).  The reference ships
+ * no kernel for this (code/kernel/setup.py:62 names per_token_quant_fp8.cu in
+ * a comment only); the arithmetic follows its FP8 convention
+ * (per_token_Mxfp4RowToBf16ToFp8Col.cu:142,161,173-177).  input bf16 [M, K],
+ * K % 8 == 0; output_q fp8 [M, K]; output_s float [M]. */
+mxb_status mxb_per_token_quant_fp8(const void* input, int64_t M, int64_t K, void* output_q,
+                                   void* output_s, float eps, mxb_stream_t stream);
+
+/* FP8 E4M3 with per-row FP32 scale -> BF16: out = bf16(float(q) * scale[row]). */
+mxb_status mxb_per_token_dequant_fp8(const void* input_q, const void* input_s, int64_t M,
+                                     int64_t K, void* output, mxb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MXFP4_B200_H_ */

@@ -1,0 +1,44 @@
+// Host-side helpers shared by the C-ABI entry points: argument checks that
+// report through mxb_last_error() instead of throwing across the C boundary.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+
+#include "mxfp4_b200.h"
+
+namespace mxb {
+
+void set_error(const char* fmt, ...);
+
+inline cudaStream_t to_cuda(mxb_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned(const void* p, uintptr_t a) {
+  return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+// Checks the launch that was just issued; returns MXB_ERR_CUDA with the CUDA
+// error text on failure.
+inline mxb_status launch_status(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("%s: CUDA launch failed: %s", what, cudaGetErrorString(e));
+    return MXB_ERR_CUDA;
+  }
+  return MXB_OK;
+}
+
+// Number of resident CTAs worth launching for a grid-stride kernel.
+int persistent_ctas(const void* kernel, int threads, size_t smem);
+
+}  // namespace mxb
+
+#define MXB_REQUIRE(cond, status, ...)  \
+  do {                                  \
+    if (!(cond)) {                      \
+      ::mxb::set_error(__VA_ARGS__);    \
+      return (status);                  \
+    }                                   \
+  } while (0)

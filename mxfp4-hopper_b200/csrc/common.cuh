@@ -1,0 +1,140 @@
+// Shared device helpers for the sm_100a MXFP4 / FP8 kernels.
+//
+// Formats (the reference's wire layout, code/kernel/per_token_quant_mxfp4.cu:256
+// and per_token_Mxfp4ToBf16_dequant.cu:22-27,137-151):
+//   * MXFP4 code byte: element 2i in the low nibble, 2i+1 in the high nibble;
+//     a nibble is s.ee.m (E2M1).
+//   * E8M0 scale byte e means 2^(e-127); the reference decodes it as the BF16
+//     bit pattern e<<7, so e = 0 reads as 0.0 and e = 255 as +Inf.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace mxb {
+
+constexpr int kSMs = 148;  // B200: 2 dies x 74 SMs
+
+// ---------------------------------------------------------------- memory
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint2 ld_stream_v2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint32_t ld_stream_u32(const void* p) {
+  uint32_t r;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint32_t ld_stream_u8(const void* p) {
+  uint32_t r;
+  asm volatile("ld.global.nc.L1::no_allocate.u8 %0, [%1];" : "=r"(r) : "l"(p));
+  return r;
+}
+// Streaming (evict-first) stores for outputs that are not re-read.
+__device__ __forceinline__ void st_stream_v4(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void st_stream_v2(void* p, uint2 v) {
+  asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
+}
+__device__ __forceinline__ void st_stream_u32(void* p, uint32_t v) {
+  asm volatile("st.global.cs.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_stream_f32(void* p, float v) {
+  asm volatile("st.global.cs.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_stream_u8(void* p, uint32_t v) {
+  asm volatile("st.global.cs.u8 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// ---------------------------------------------------------------- bit ops
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+// Per-16-bit-lane unsigned maximum.
+__device__ __forceinline__ uint32_t vmax_u16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ float bf16lo_to_f(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi_to_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// ---------------------------------------------------------------- conversions
+// Four float pairs -> four E2M1x2 bytes, round-to-nearest-even, saturating to
+// +-6 (Blackwell cvt.rn.satfinite.e2m1x2.f32).  v[2i] lands in the low nibble.
+__device__ __forceinline__ uint32_t cvt_e2m1x8(const float v[8]) {
+  uint32_t r;
+  asm("{\n"
+      ".reg .b8 b0, b1, b2, b3;\n"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n"
+      "mov.b32 %0, {b0, b1, b2, b3};\n"
+      "}"
+      : "=r"(r)
+      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
+  return r;
+}
+// Two floats -> two E4M3 bytes (lo = a, hi = b), RNE, saturating to +-448;
+// this is the conversion __nv_fp8_e4m3(float) performs on sm_89 and later.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float a, float b) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
+  return r;
+}
+// Two floats -> BF16x2 (lo = a, hi = b), RNE; NaN becomes canonical 0x7FFF.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// ---------------------------------------------------------------- E2M1 decode
+// BF16 bit patterns of the eight E2M1 magnitudes {0,.5,1,1.5,2,3,4,6}, split
+// into byte tables so that `prmt` can look up four nibbles at once.
+//   low bytes : 00 00 80 C0 00 40 80 C0
+//   high bytes: 00 3F 3F 3F 40 40 40 40
+constexpr uint32_t kE2m1Lo0 = 0xC0800000u, kE2m1Lo1 = 0xC0804000u;
+constexpr uint32_t kE2m1Hi0 = 0x3F3F3F00u, kE2m1Hi1 = 0x40404040u;
+
+// Decode the four nibbles in the low 16 bits of `w` into two BF16x2 words
+// (unscaled E2M1 values, sign included): out0 = {e0, e1}, out1 = {e2, e3}.
+// Bit-identical to the reference's shift/add decode
+// (per_token_Mxfp4ToBf16_dequant.cu:137-151), including -0 for code 8.
+__device__ __forceinline__ void e2m1x4_to_bf16x4(uint32_t w, uint32_t& out0, uint32_t& out1) {
+  const uint32_t sel = w & 0x7777u;
+  const uint32_t lo = prmt(kE2m1Lo0, kE2m1Lo1, sel);
+  uint32_t hi = prmt(kE2m1Hi0, kE2m1Hi1, sel);
+  // sign bits (bit 3 of each nibble) -> 0x80 in the matching high byte
+  const uint32_t sgn = prmt(0x00008000u, 0u, ((w >> 3) & 0x1111u));
+  hi |= sgn;
+  out0 = prmt(lo, hi, 0x5140u);
+  out1 = prmt(lo, hi, 0x7362u);
+}
+
+// E8M0 byte -> float via the reference's BF16 reinterpretation.
+__device__ __forceinline__ float e8m0_to_f(uint32_t e) { return __uint_as_float(e << 23); }
+
+__host__ __device__ __forceinline__ int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace mxb

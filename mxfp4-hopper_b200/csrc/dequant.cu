@@ -1,0 +1,189 @@
+// MXFP4 -> BF16 dequantize and MXFP4 -> FP8 E4M3 rowwise convert for sm_100a.
+//
+// DQ-bf16 contract (code/kernel/per_token_Mxfp4ToBf16_dequant.cu:129-156):
+//   out = bf16_rn(float(e2m1(nibble)) * float(bf16 bits e<<7))
+// The product of an E2M1 value and a power of two is exact in BF16 except on
+// overflow (-> Inf, as the float path rounds) and for e in {0, 1, 255}
+// (zero / subnormal / Inf-NaN scales), which take the float path.  Everything
+// else is one BF16x2 multiply per two outputs.
+//
+// DQ-fp8-row contract (code/kernel/per_token_Mxfp4ToFp8.cu:157-233), per 1x128
+// group of four E8M0 bytes:
+//   g   = (uint16)(max e - 6)       group scale float bits ((uint8)g) << 23
+//   adj = (uint16)(g - e)
+//   q   = E4M3(clamp(bf16(code_bits - (adj << 7) mod 2^16), +-448))
+// which re-bases every block onto the group exponent in integer arithmetic;
+// zero codes in blocks more than six binades below the group maximum wrap to
+// +-448 exactly as on the reference.
+#include "capi_util.h"
+#include "common.cuh"
+
+namespace mxb {
+namespace {
+
+// ------------------------------------------------------------------ DQ-bf16
+// A lane turns 4 code bytes (8 elements) into one 16-byte BF16 store, so each
+// warp instruction reads 128 contiguous code bytes and writes 512 contiguous
+// output bytes.  Four chunks per lane are in flight per iteration.
+constexpr int kDqUnroll = 4;
+
+__device__ __forceinline__ uint4 dq_bf16_chunk(uint32_t w, uint32_t e) {
+  uint32_t o[4];
+  e2m1x4_to_bf16x4(w, o[0], o[1]);
+  e2m1x4_to_bf16x4(w >> 16, o[2], o[3]);
+  if (e - 2u <= 252u) {  // e in [2, 254]: exact BF16 product
+    const uint32_t s2 = (e << 7) | (e << 23);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = mul_bf16x2(o[i], s2);
+  } else {
+    const float s = e8m0_to_f(e);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = cvt_bf16x2(bf16lo_to_f(o[i]) * s, bf16hi_to_f(o[i]) * s);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__global__ void __launch_bounds__(256) dq_bf16_kernel(const uint8_t* __restrict__ codes,
+                                                      const uint8_t* __restrict__ scales,
+                                                      int64_t chunks, uint8_t* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * kDqUnroll;
+  for (int64_t base = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) * kDqUnroll;
+       base < chunks; base += stride) {
+    uint32_t w[kDqUnroll], e[kDqUnroll];
+#pragma unroll
+    for (int k = 0; k < kDqUnroll; ++k) {
+      const int64_t c = base + k * 32 + lane;
+      if (c < chunks) {
+        w[k] = ld_stream_u32(codes + c * 4);
+        e[k] = ld_stream_u8(scales + (c >> 2));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kDqUnroll; ++k) {
+      const int64_t c = base + k * 32 + lane;
+      if (c < chunks) st_stream_v4(out + c * 16, dq_bf16_chunk(w[k], e[k]));
+    }
+  }
+}
+
+// -------------------------------------------------------------- DQ-fp8-row
+// A lane converts 8 code bytes (16 elements, half a 32-element block) into one
+// 16-byte FP8 store; eight lanes cover one 1x128 group and read the group's
+// four E8M0 bytes as one word.
+__device__ __forceinline__ uint32_t max_u8x4(uint32_t s) {
+  uint32_t a = max(s & 0xFFu, (s >> 8) & 0xFFu);
+  uint32_t b = max((s >> 16) & 0xFFu, s >> 24);
+  return max(a, b);
+}
+
+__device__ __forceinline__ uint32_t rebase_fp8x2(uint32_t x2, uint32_t off16) {
+  // x2: two BF16 code patterns; returns E4M3 of both re-based values
+  float lo = __uint_as_float((x2 << 16) - off16);
+  float hi = __uint_as_float((x2 & 0xFFFF0000u) - off16);
+  lo = fmaxf(-448.0f, fminf(448.0f, lo));
+  hi = fmaxf(-448.0f, fminf(448.0f, hi));
+  return cvt_e4m3x2(lo, hi);
+}
+
+__global__ void __launch_bounds__(256) dq_fp8_row_kernel(const uint8_t* __restrict__ codes,
+                                                         const uint8_t* __restrict__ scales,
+                                                         int64_t M, int64_t Kb,
+                                                         uint8_t* __restrict__ out,
+                                                         float* __restrict__ scales_out) {
+  const int64_t lanes_total = M * Kb / 8;  // one lane per 8 code bytes
+  const int64_t groups_per_row = Kb / 64;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 2;
+  for (int64_t base = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) * 2;
+       base < lanes_total; base += stride) {
+    uint2 w[2];
+    uint32_t sw[2], e[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int64_t l = base + k * 32 + (threadIdx.x & 31);
+      if (l < lanes_total) {
+        w[k] = ld_stream_v2(codes + l * 8);
+        sw[k] = ld_stream_u32(scales + (l >> 3) * 4);
+        e[k] = (sw[k] >> (8 * ((l >> 1) & 3))) & 0xFFu;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int64_t l = base + k * 32 + (threadIdx.x & 31);
+      if (l >= lanes_total) continue;
+      const uint32_t mx = max_u8x4(sw[k]);
+      const uint32_t g = (mx - 6u) & 0xFFFFu;
+      const uint32_t adj = (g - e[k]) & 0xFFFFu;
+      const uint32_t off16 = ((adj << 7) & 0xFFFFu) << 16;
+      uint32_t o[4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t cw = h ? w[k].y : w[k].x;
+        uint32_t x0, x1, x2, x3;
+        e2m1x4_to_bf16x4(cw, x0, x1);
+        e2m1x4_to_bf16x4(cw >> 16, x2, x3);
+        o[2 * h] = rebase_fp8x2(x0, off16) | (rebase_fp8x2(x1, off16) << 16);
+        o[2 * h + 1] = rebase_fp8x2(x2, off16) | (rebase_fp8x2(x3, off16) << 16);
+      }
+      st_stream_v4(out + l * 16, make_uint4(o[0], o[1], o[2], o[3]));
+      if ((l & 7) == 0) {
+        const int64_t grp = l >> 3;
+        const int64_t r = grp / groups_per_row, gc = grp - r * groups_per_row;
+        scales_out[gc * M + r] = __uint_as_float((g & 0xFFu) << 23);
+      }
+    }
+  }
+}
+
+int grid_for(const void* kern, int64_t work_lanes, int per_lane) {
+  const int64_t want = cdiv(work_lanes, 256LL * per_lane);
+  const int64_t cap = (int64_t)persistent_ctas(kern, 256, 0) * 2;
+  return (int)(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+}  // namespace
+}  // namespace mxb
+
+using namespace mxb;
+
+extern "C" mxb_status mxb_per_token_Mxfp4ToBf16_dequant(const void* input, const void* input_s,
+                                                        int64_t M, int64_t Kb, void* output,
+                                                        mxb_stream_t stream) {
+  MXB_REQUIRE(M >= 0 && Kb >= 0 && Kb % 16 == 0, MXB_ERR_INVALID_ARGUMENT,
+              "dequant_bf16: need Kb %% 16 == 0 (one E8M0 byte per 16 code bytes), got %lld",
+              (long long)Kb);
+  if (M == 0 || Kb == 0) return MXB_OK;
+  MXB_REQUIRE(input && input_s && output, MXB_ERR_INVALID_ARGUMENT, "dequant_bf16: null pointer");
+  MXB_REQUIRE(aligned(input, 4) && aligned(output, 16), MXB_ERR_MISALIGNED,
+              "dequant_bf16: input must be 4-byte and output 16-byte aligned");
+  const int64_t chunks = M * Kb / 4;
+  const int grid = grid_for((const void*)dq_bf16_kernel, chunks, kDqUnroll);
+  dq_bf16_kernel<<<grid, 256, 0, to_cuda(stream)>>>((const uint8_t*)input, (const uint8_t*)input_s,
+                                                    chunks, (uint8_t*)output);
+  return launch_status("dequant_bf16");
+}
+
+extern "C" mxb_status mxb_per_token_Mxfp4ToFp8(const void* input, const void* input_s, int64_t M,
+                                               int64_t Kb, void* output_q, void* output_s,
+                                               mxb_stream_t stream) {
+  MXB_REQUIRE(M >= 0 && Kb >= 0 && Kb % 64 == 0, MXB_ERR_INVALID_ARGUMENT,
+              "mxfp4_to_fp8: need Kb %% 64 == 0 (1x128 groups), got %lld", (long long)Kb);
+  if (M == 0 || Kb == 0) return MXB_OK;
+  MXB_REQUIRE(input && input_s && output_q && output_s, MXB_ERR_INVALID_ARGUMENT,
+              "mxfp4_to_fp8: null pointer");
+  MXB_REQUIRE(aligned(input, 8) && aligned(input_s, 4) && aligned(output_q, 16) &&
+                  aligned(output_s, 4),
+              MXB_ERR_MISALIGNED, "mxfp4_to_fp8: misaligned pointer");
+  const int64_t lanes = M * Kb / 8;
+  const int grid = grid_for((const void*)dq_fp8_row_kernel, lanes, 2);
+  dq_fp8_row_kernel<<<grid, 256, 0, to_cuda(stream)>>>((const uint8_t*)input,
+                                                       (const uint8_t*)input_s, M, Kb,
+                                                       (uint8_t*)output_q, (float*)output_s);
+  return launch_status("mxfp4_to_fp8");
+}
+
+extern "C" mxb_status mxb_per_token_Mxfp4ToBf16ToFp8(const void* input, const void* input_s,
+                                                     int64_t M, int64_t Kb, void* output_q,
+                                                     void* output_s, mxb_stream_t stream) {
+  return mxb_per_token_Mxfp4ToFp8(input, input_s, M, Kb, output_q, output_s, stream);
+}

@@ -1,0 +1,86 @@
+"""ctypes binding of the C ABI (include/mxfp4_b200.h) of libmxfp4_b200.so.
+
+This is how Python code outside torch (tests, the benchmark's end-to-end leg,
+an FFI user) reaches the CUDA kernels: raw device pointers, sizes and a stream
+handle, no torch types.  Loading fails loudly when the library has not been
+built; there is no fallback implementation.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent.parent
+LIB_PATH = PKG / "lib" / "libmxfp4_b200.so"
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+_F = ctypes.c_float
+
+# name -> argument types (all return mxb_status as int)
+SIGNATURES = {
+    "mxb_per_token_group_quant_fp4": [_P, _I64, _I64, _I64, _P, _P, _I, _F, _F, _F, _I, _P],
+    "mxb_quant_mxfp4_rowcol": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _F, _F, _F, _P],
+    "mxb_swizzle_scales": [_P, _I64, _I64, _P, _P],
+    "mxb_per_token_Mxfp4ToBf16_dequant": [_P, _P, _I64, _I64, _P, _P],
+    "mxb_per_token_Mxfp4ToFp8": [_P, _P, _I64, _I64, _P, _P, _P],
+    "mxb_per_token_Mxfp4ToBf16ToFp8": [_P, _P, _I64, _I64, _P, _P, _P],
+    "mxb_per_token_Mxfp4ToFp8_col": [_P, _P, _I64, _I64, _P, _P, _P],
+    "mxb_per_token_Mxfp4RowToBf16ToFp8Col": [_P, _P, _I64, _I64, _P, _P, _F, _P],
+    "mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit": [_P, _P, _I64, _I64, _P, _P, _P, _P, _P,
+                                                    _I64, _I64, _F, _P],
+    "mxb_per_token_quant_fp8": [_P, _I64, _I64, _P, _P, _F, _P],
+    "mxb_per_token_dequant_fp8": [_P, _P, _I64, _I64, _P, _P],
+}
+
+STATUS = {0: "MXB_OK", 1: "MXB_ERR_INVALID_ARGUMENT", 2: "MXB_ERR_MISALIGNED", 3: "MXB_ERR_CUDA",
+          4: "MXB_ERR_UNSUPPORTED"}
+
+
+class MxbError(RuntimeError):
+    def __init__(self, fn: str, status: int, msg: str):
+        super().__init__(f"{fn} -> {STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load libmxfp4_b200.so and declare every exported entry point."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is missing: build it with "
+                              "`python mxfp4-hopper_b200/build.py` (no CPU fallback exists)")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, args in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_int
+        L.mxb_last_error.restype = ctypes.c_char_p
+        L.mxb_version.restype = ctypes.c_char_p
+        _lib = L
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    """Call an entry point and raise MxbError on a non-OK status."""
+    L = load()
+    st = getattr(L, name)(*args)
+    if st != 0:
+        raise MxbError(name, st, L.mxb_last_error().decode())
+
+
+def status_of(name: str, *args) -> int:
+    """Call an entry point and return its raw status (for error-path tests)."""
+    return int(getattr(load(), name)(*args))
+
+
+def last_error() -> str:
+    return load().mxb_last_error().decode()
+
+
+def version() -> str:
+    return load().mxb_version().decode()

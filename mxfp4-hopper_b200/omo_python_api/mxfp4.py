@@ -1,0 +1,123 @@
+"""MXFP4 quantize wrappers (reference: code/kernel/api/mxfp4.py).
+
+Outputs are allocated here and filled by the sm_100a kernels through `omo`.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+import mxfp4_b200  # noqa: F401
+from omo import omo_per_token_group_quant_fp4, omo_quant_mxfp4_rowcol
+
+fp8_type_ = torch.float8_e4m3fn
+uint8_type = torch.uint8
+fp8_max = torch.finfo(fp8_type_).max
+fp8_min = -fp8_max
+mxfp4_max = 6.0
+mxfp4_min = -mxfp4_max
+FLOAT4_E2M1_MAX = 6.0
+FLOAT8_E4M3_MAX = torch.finfo(torch.float8_e4m3fn).max
+
+
+def align(x: int, y: int) -> int:
+    return (x + y - 1) // y * y
+
+
+def create_per_token_group_quant_fp8_output_scale(x_shape, device, group_size,
+                                                  column_major_scales: bool,
+                                                  scale_tma_aligned: bool, scale_ue8m0: bool):
+    """Scale tensor for a quantize call (api/mxfp4.py:133-161).
+
+    With scale_ue8m0 the reference builds a column-major packed int32 layout that
+    its kernel path asserts against; the row-major uint8 [rows, cols] layout is
+    the one every caller uses."""
+    if scale_ue8m0:
+        assert column_major_scales and scale_tma_aligned
+        *x_batch, x_q_mn, x_q_k = x_shape
+        x_s_mn, x_s_k = x_q_mn, x_q_k // 128
+        aligned_mn = align(x_s_mn, 4)
+        aligned_k = align(x_s_k, 4)
+        return torch.empty((*x_batch, aligned_k // 4, aligned_mn), device=device,
+                           dtype=torch.int).transpose(-1, -2)[..., :x_s_mn, :]
+    return torch.empty((x_shape[0], x_shape[1]), device=device, dtype=torch.uint8)
+
+
+def omo_per_token_group_quant_fp4_warpper(x: torch.Tensor, group_size: int, eps: float = 1e-10,
+                                          column_major_scales: bool = False,
+                                          scale_tma_aligned: bool = False,
+                                          scale_ue8m0: bool = False,
+                                          fuse_silu_and_mul: bool = False,
+                                          masked_m: Optional[torch.Tensor] = None,
+                                          enable_v2: Optional[bool] = None):
+    """api/mxfp4.py:91-127 (the scale tensor is sized from the code shape, as there)."""
+    assert x.shape[-1] % group_size == 0, \
+        "the last dimension of `x` cannot be divisible by `group_size`"
+    assert x.is_contiguous(), "`x` is not contiguous"
+    out_shape = (*x.shape[:-1], x.shape[-1] // 2)
+    x_q = torch.empty(out_shape, device=x.device, dtype=uint8_type)
+    x_s = create_per_token_group_quant_fp8_output_scale(
+        x_shape=out_shape, device=x.device, group_size=group_size,
+        column_major_scales=column_major_scales, scale_tma_aligned=scale_tma_aligned,
+        scale_ue8m0=scale_ue8m0)
+    if x.shape[0] > 0:
+        omo_per_token_group_quant_fp4(x, x_q, x_s, group_size, eps, mxfp4_min, mxfp4_max,
+                                      scale_ue8m0)
+    return x_q, x_s
+
+
+def omo_per_token_group_quant_4bit_warpper(x: torch.Tensor, group_size: int,
+                                           dst_dtype: torch.dtype, eps: float = 1e-10,
+                                           column_major_scales: bool = False,
+                                           scale_tma_aligned: bool = False,
+                                           scale_ue8m0: bool = False,
+                                           fuse_silu_and_mul: bool = False,
+                                           masked_m: Optional[torch.Tensor] = None,
+                                           enable_v2: Optional[bool] = None):
+    """api/mxfp4.py:63-90: forwards to the FP4 wrapper."""
+    return omo_per_token_group_quant_fp4_warpper(
+        x=x, group_size=group_size, eps=eps, column_major_scales=column_major_scales,
+        scale_tma_aligned=scale_tma_aligned, scale_ue8m0=scale_ue8m0,
+        fuse_silu_and_mul=fuse_silu_and_mul, masked_m=masked_m, enable_v2=enable_v2)
+
+
+def omo_per_token_group_quant_mxfp4(x: torch.Tensor):
+    """Rowwise MXFP4 quantize (api/mxfp4.py:164-202): codes [..., K/2] uint8 and
+    E8M0 scales [rows, K/32] uint8 (leading dimensions flattened into rows)."""
+    group_size = 32
+    assert x.shape[-1] % group_size == 0, \
+        "the last dimension of `x` cannot be divisible by `group_size`"
+    assert x.is_contiguous(), "`x` is not contiguous"
+    out_shape = (*x.shape[:-1], x.shape[-1] // 2)
+    rows = x.numel() // x.shape[-1] if x.shape[-1] else 0
+    x_q = torch.empty(out_shape, device=x.device, dtype=uint8_type)
+    x_s = torch.empty((rows, x.shape[-1] // 32), device=x.device, dtype=torch.uint8)
+    if x.shape[0] > 0:
+        omo_per_token_group_quant_fp4(x, x_q, x_s, group_size, 1e-10, mxfp4_min, mxfp4_max, False)
+    return x_q, x_s
+
+
+def omo_per_token_group_quant_mxfp4_rowcol(x: torch.Tensor, rowwise: bool = True,
+                                           swizzled_scales: bool = False):
+    """Rowwise and columnwise MXFP4 quantize of a 2-D tensor in one pass.
+
+    Same bytes as `omo_per_token_group_quant_mxfp4(x)` plus
+    `omo_per_token_group_quant_mxfp4(x.T.contiguous())` (the Transformer Engine
+    quantize, transformer_engine-2.8.diff:1464-1466), without the transpose copy.
+    Returns (codes_row, scales_row, codes_col, scales_col[, scales_row_swizzled]);
+    the row pair is None when rowwise=False."""
+    assert x.dim() == 2 and x.is_contiguous()
+    M, K = x.shape
+    dev = x.device
+    cr = torch.empty((M, K // 2), device=dev, dtype=torch.uint8) if rowwise else \
+        torch.empty(0, device=dev, dtype=torch.uint8)
+    sr = torch.empty((M, K // 32), device=dev, dtype=torch.uint8) if rowwise else \
+        torch.empty(0, device=dev, dtype=torch.uint8)
+    cc = torch.empty((K, M // 2), device=dev, dtype=torch.uint8)
+    sc = torch.empty((K, M // 32), device=dev, dtype=torch.uint8)
+    swz = torch.empty((align(M, 128), align(K // 32, 4)), device=dev, dtype=torch.uint8) \
+        if swizzled_scales else None
+    omo_quant_mxfp4_rowcol(x, cr, sr, cc, sc, swz)
+    out = (cr if rowwise else None, sr if rowwise else None, cc, sc)
+    return out + (swz,) if swizzled_scales else out

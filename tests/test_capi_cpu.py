@@ -1,0 +1,58 @@
+"""CPU-only checks of the C ABI: the library loads, exports every entry point
+include/*.h declares, and rejects out-of-contract arguments with a status and
+a message before touching the GPU."""
+import re
+from pathlib import Path
+
+import pytest
+
+from mxfp4_b200 import capi
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    names = []
+    for h in sorted((ROOT / "include").glob("*.h")):
+        txt = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names += re.findall(r"^\s*(?:mxb_status|const char\s*\*)\s*(mxb_\w+)\s*\(", txt, flags=re.M)
+    return names
+
+
+def test_library_loads_and_reports_version():
+    assert "sm_100a" in capi.version()
+
+
+def test_every_declared_symbol_is_exported():
+    L = capi.load()
+    names = declared_symbols()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(L, n), f"{n} declared in include/ but not exported"
+    for n in capi.SIGNATURES:
+        assert n in names, f"{n} bound in capi.py but not declared in include/"
+
+
+@pytest.mark.parametrize("name,args,status", [
+    ("mxb_per_token_group_quant_fp4", (1, 4, 40, 40, 1, 1, 32, 1e-10, -6.0, 6.0, 0, None), 1),
+    ("mxb_per_token_group_quant_fp4", (1, 4, 64, 64, 1, 1, 16, 1e-10, -6.0, 6.0, 0, None), 4),
+    ("mxb_per_token_group_quant_fp4", (1, 4, 64, 64, 1, 1, 32, 1e-10, -6.0, 6.0, 1, None), 4),
+    ("mxb_per_token_group_quant_fp4", (1, 4, 64, 60, 1, 1, 32, 1e-10, -6.0, 6.0, 0, None), 2),
+    ("mxb_quant_mxfp4_rowcol", (1, 48, 64, 64, 1, 1, 1, 1, None, 1e-10, -6.0, 6.0, None), 1),
+    ("mxb_quant_mxfp4_rowcol", (1, 64, 64, 64, 1, None, 1, 1, None, 1e-10, -6.0, 6.0, None), 1),
+    ("mxb_per_token_Mxfp4ToBf16_dequant", (1, 1, 4, 24, 1, None), 1),
+    ("mxb_per_token_Mxfp4ToFp8", (1, 1, 4, 96, 1, 1, None), 1),
+    ("mxb_per_token_Mxfp4ToFp8_col", (1, 1, 64, 128, 1, 1, None), 1),
+    ("mxb_per_token_Mxfp4RowToBf16ToFp8Col", (1, 1, 4, 48, 1, 1, 1e-10, None), 1),
+    ("mxb_per_token_quant_fp8", (1, 4, 12, 1, 1, 1e-10, None), 1),
+    ("mxb_per_token_dequant_fp8", (1, 1, 4, 24, 1, None), 1),
+])
+def test_out_of_contract_arguments_are_rejected(name, args, status):
+    assert capi.status_of(name, *args) == status
+    assert capi.last_error()
+
+
+def test_empty_inputs_are_a_no_op():
+    assert capi.status_of("mxb_per_token_group_quant_fp4", None, 0, 64, 64, None, None, 32, 1e-10,
+                          -6.0, 6.0, 0, None) == 0
+    assert capi.status_of("mxb_per_token_Mxfp4ToBf16_dequant", None, None, 0, 16, None, None) == 0
