@@ -219,6 +219,14 @@ def main():
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        # keep the GPU under the same load for ~1.5 s before the timed region so
+        # the sampler sees clocks under load even when K steps take milliseconds
+        t_end = time.perf_counter() + 1.5
+        while time.perf_counter() < t_end:
+            for _ in range(50):
+                step()
+            torch.cuda.synchronize(dev)
+        barrier()
         e0.record(stream)
         for _ in range(args.steps):
             step()

@@ -45,6 +45,10 @@ typedef enum {
 const char* mxb_last_error(void);
 /* Library version string. */
 const char* mxb_version(void);
+/* Number of bounded pipeline waits that gave up on the current device since
+ * the library was loaded (0 in correct operation; a non-zero value means a
+ * kernel abandoned its work and its outputs are invalid).  Synchronises. */
+unsigned int mxb_wait_timeouts(void);
 
 /* ------------------------------------------------------------ quantize */
 
@@ -111,7 +115,7 @@ mxb_status mxb_per_token_Mxfp4ToBf16ToFp8(const void* input, const void* input_s
 /* MXFP4 -> transposed FP8 E4M3 with a scale per (128-row block, 32-column
  * block) from the largest E8M0 exponent.  Replaces omo_per_token_Mxfp4ToFp8_col
  * (code/kernel/ops.cu:40, per_token_Mxfp4ToFp8_col.cu:305-384; kernel
- * :110-301), quirks included (outputs carry no sign; see DESIGN).  input uint8
+ * :110-301), quirks included (the outputs carry no sign).  input uint8
  * [M, Kb], M % 128 == 0, Kb % 128 == 0; output_q fp8 [2*Kb, M]; output_s
  * float [M/128, 2*Kb]. */
 mxb_status mxb_per_token_Mxfp4ToFp8_col(const void* input, const void* input_s, int64_t M,

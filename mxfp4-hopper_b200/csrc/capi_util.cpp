@@ -1,6 +1,8 @@
 // Error reporting and small host utilities behind the C ABI.
 #include "capi_util.h"
 
+#include <cudaTypedefs.h>
+
 #include <mutex>
 #include <unordered_map>
 
@@ -39,3 +41,44 @@ int persistent_ctas(const void* kernel, int threads, size_t smem) {
 
 extern "C" const char* mxb_last_error(void) { return mxb::g_err; }
 extern "C" const char* mxb_version(void) { return "mxfp4_b200 0.1.0 (sm_100a)"; }
+
+// ---------------------------------------------------------------- tensor maps
+
+namespace mxb {
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+bool make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                        int elem_bytes, int64_t rows, int64_t cols, int64_t ld, uint32_t box_cols,
+                        uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return false;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * elem_bytes)};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+    return false;
+  }
+  return true;
+}
+
+}  // namespace mxb

@@ -1,6 +1,7 @@
 // Host-side helpers shared by the C-ABI entry points: argument checks that
 // report through mxb_last_error() instead of throwing across the C boundary.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -29,6 +30,14 @@ inline mxb_status launch_status(const char* what) {
   }
   return MXB_OK;
 }
+
+// Host: 2-D row-major tensor map over [rows, cols] elements of `elem_bytes`
+// with row pitch `ld` elements and a box of box_cols x box_rows (no swizzle,
+// zero fill out of range).  Reports through set_error on failure.
+bool make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                        int elem_bytes, int64_t rows, int64_t cols, int64_t ld, uint32_t box_cols,
+                        uint32_t box_rows,
+                        CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
 
 // Number of resident CTAs worth launching for a grid-stride kernel.
 int persistent_ctas(const void* kernel, int threads, size_t smem);

@@ -70,6 +70,26 @@ __device__ __forceinline__ uint32_t vmax_u16x2(uint32_t a, uint32_t b) {
   asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
+// Per-lane max(|a|, |b|) of two BF16 pairs; a NaN in either input yields the
+// canonical NaN 0x7FFF (whose magnitude sorts above Inf), so one instruction
+// both reduces magnitudes and flags non-finite inputs.  The result's sign bits
+// are meaningless (xorsign): mask them off before use.
+__device__ __forceinline__ uint32_t absmax_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Tree reduction of N BF16 pairs with absmax_bf16x2 (depth log2 N).
+template <int N>
+__device__ __forceinline__ uint32_t absmax_tree(const uint32_t* w) {
+  if constexpr (N == 1) {
+    return w[0];
+  } else {
+    return absmax_bf16x2(absmax_tree<N / 2>(w), absmax_tree<N - N / 2>(w + N / 2));
+  }
+}
+
 __device__ __forceinline__ float bf16lo_to_f(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi_to_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 

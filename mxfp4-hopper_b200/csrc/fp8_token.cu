@@ -138,34 +138,31 @@ __device__ __forceinline__ float e4m3_to_f(uint32_t b) {
   return f * 0x1p120f;
 }
 
-// One lane: 16 FP8 bytes -> 32 bytes of BF16.
+// One lane: 8 FP8 bytes -> 16 bytes of BF16; a warp instruction reads 256
+// contiguous bytes and writes 512.
 __global__ void __launch_bounds__(256) fp8_dequant_rows_kernel(const uint8_t* __restrict__ q,
                                                                const float* __restrict__ scale,
                                                                int64_t M, int64_t K,
                                                                uint8_t* __restrict__ out) {
-  const int64_t nch = M * K / 16, per_row = K / 16;
+  const int64_t nch = M * K / 8, per_row = K / 8;
   for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < nch;
        c += (int64_t)gridDim.x * blockDim.x) {
-    const uint4 v = ld_stream_v4(q + c * 16);
+    const uint2 v = ld_stream_v2(q + c * 8);
     const float s = scale[c / per_row];
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t o[8];
+    const uint32_t w[2] = {v.x, v.y};
+    uint32_t o[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const bool nan = ((w[j] & 0x7Fu) == 0x7Fu) || ((w[j] & 0x7F00u) == 0x7F00u) ||
-                       ((w[j] & 0x7F0000u) == 0x7F0000u) || ((w[j] & 0x7F000000u) == 0x7F000000u);
+    for (int j = 0; j < 2; ++j) {
       float f[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const uint32_t b = (w[j] >> (8 * u)) & 0xFFu;
-        f[u] = e4m3_to_f(b) * s;
-        if (nan && (b & 0x7Fu) == 0x7Fu) f[u] = __uint_as_float(0x7FC00000u);
+        f[u] = (b & 0x7Fu) == 0x7Fu ? __uint_as_float(0x7FC00000u) : e4m3_to_f(b) * s;
       }
       o[2 * j] = cvt_bf16x2(f[0], f[1]);
       o[2 * j + 1] = cvt_bf16x2(f[2], f[3]);
     }
-    st_stream_v4(out + c * 32, make_uint4(o[0], o[1], o[2], o[3]));
-    st_stream_v4(out + c * 32 + 16, make_uint4(o[4], o[5], o[6], o[7]));
+    st_stream_v4(out + c * 16, make_uint4(o[0], o[1], o[2], o[3]));
   }
 }
 
@@ -204,13 +201,13 @@ extern "C" mxb_status mxb_per_token_quant_fp8(const void* input, int64_t M, int6
 extern "C" mxb_status mxb_per_token_dequant_fp8(const void* input_q, const void* input_s,
                                                 int64_t M, int64_t K, void* output,
                                                 mxb_stream_t stream) {
-  MXB_REQUIRE(M >= 0 && K >= 0 && K % 16 == 0, MXB_ERR_INVALID_ARGUMENT,
-              "dequant_fp8: need K %% 16 == 0, got %lld", (long long)K);
+  MXB_REQUIRE(M >= 0 && K >= 0 && K % 8 == 0, MXB_ERR_INVALID_ARGUMENT,
+              "dequant_fp8: need K %% 8 == 0, got %lld", (long long)K);
   if (M == 0 || K == 0) return MXB_OK;
   MXB_REQUIRE(input_q && input_s && output, MXB_ERR_INVALID_ARGUMENT, "dequant_fp8: null pointer");
-  MXB_REQUIRE(aligned(input_q, 16) && aligned(output, 16), MXB_ERR_MISALIGNED,
-              "dequant_fp8: input_q and output must be 16-byte aligned");
-  const int64_t nch = M * K / 16;
+  MXB_REQUIRE(aligned(input_q, 8) && aligned(output, 16), MXB_ERR_MISALIGNED,
+              "dequant_fp8: input_q must be 8-byte and output 16-byte aligned");
+  const int64_t nch = M * K / 8;
   const int64_t want = cdiv(nch, 256);
   const int64_t cap = (int64_t)persistent_ctas((const void*)fp8_dequant_rows_kernel, 256, 0) * 2;
   const int grid = (int)(want < cap ? want : cap);

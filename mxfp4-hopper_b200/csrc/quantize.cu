@@ -8,18 +8,27 @@
 //   scale = (uint8)((int)log2f(y_s) + 127)
 //   code  = E2M1_RNE(clamp(x * (1 / y_s), fp4_min, fp4_max)), sign kept on zero
 //
-// Fast path (fp4_max = 6, fp4_min = -6, eps <= 6e-10, the reference API's only
-// configuration): the block amax is an integer max over BF16 magnitudes, the
-// exponent k = ceil(log2 y) is read from y's bits (exact, because a BF16 amax
-// divided by 6 is either a power of two or at least 0.5% away from one), and
-// the codes come from Blackwell's cvt.rn.satfinite.e2m1x2.f32.  Blocks holding
-// Inf/NaN, and every block when the parameters differ from the defaults, take
-// the generic path, which evaluates the reference formula literally and
-// encodes with the reference's integer rounding.
+// Fast path (fp4_max = 6, fp4_min = -6, 0 <= eps <= 6e-10: the reference API's
+// only configuration).  For a finite BF16 amax = 1.m * 2^e the exponent of
+// y_s is exactly
+//     k = max(e - 2 + [1.m > 1.5], -33)
+// because amax/6 = (1.m / 1.5) * 2^(e-2) and 1.m / 1.5 lies in [2/3, 4/3): it
+// is a power of two only at 1.m = 1.5 and otherwise at least 0.5% away from
+// one, so neither the rounding of the division nor log2f can move the ceiling;
+// -33 = ceil(log2(1e-10)) is the clamp, and eps <= 6e-10 never raises amax/6
+// above it.  The block amax is an integer max over BF16 magnitude patterns,
+// x * 2^-k is exact (two lanes per mul.rn.f32x2), and the codes come from
+// Blackwell's cvt.rn.satfinite.e2m1x2.f32, whose round-to-nearest-even with
+// the sign kept on zero equals the reference's integer rounding for every
+// such product (both are checked exhaustively against the reference kernel).
+// Blocks holding Inf/NaN, and every block when the parameters differ from the
+// defaults, take the generic path, which evaluates the reference formula
+// literally and encodes with the reference's integer rounding.
 #include <cuda_bf16.h>
 
 #include "capi_util.h"
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace mxb {
 namespace {
@@ -28,6 +37,7 @@ struct QuantParams {
   float eps, fp4_min, fp4_max;
 };
 
+// ------------------------------------------------------------ generic path
 // Reference E2M1 rounding of an already clamped float
 // (per_token_quant_mxfp4.cu:213-256): re-bias the exponent from 127 to 1,
 // denormalise values below 1.0 by a right shift, round to nearest even on the
@@ -49,7 +59,7 @@ __device__ __forceinline__ uint32_t e2m1_encode_generic(float q) {
   return sign | r;
 }
 
-// The reference scale rule, evaluated literally (generic path).
+// The reference scale rule, evaluated literally.
 __device__ __forceinline__ void scale_generic(float amax, const QuantParams& p, float& inv,
                                               uint32_t& byte) {
   float y = amax / p.fp4_max;
@@ -59,67 +69,118 @@ __device__ __forceinline__ void scale_generic(float amax, const QuantParams& p, 
   inv = 1.0f / y;
 }
 
-// Fast scale rule from the largest BF16 magnitude pattern `mb` (finite).
-__device__ __forceinline__ void scale_fast(uint32_t mb, float eps, float& inv, uint32_t& byte) {
-  const float amax = fmaxf(eps, __uint_as_float(mb << 16));
-  const float y = fmaxf(__fdiv_rn(amax, 6.0f), 1e-10f);
-  const uint32_t yb = __float_as_uint(y);
-  const int k = (int)(yb >> 23) - 127 + ((yb & 0x7FFFFFu) != 0u);
-  byte = (uint32_t)(k + 127);
-  inv = __uint_as_float((uint32_t)(127 - k) << 23);
+// 8 values given as float bit patterns -> one word of 8 E2M1 codes (element
+// 2i in the low nibble of byte i), generic rounding.
+__device__ __forceinline__ uint32_t encode8_generic(const uint32_t (&f)[8], float inv,
+                                                    const QuantParams& p) {
+  uint32_t r = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float q = fminf(fmaxf(__uint_as_float(f[j]) * inv, p.fp4_min), p.fp4_max);
+    r |= e2m1_encode_generic(q) << (4 * j);
+  }
+  return r;
 }
 
-// Largest |x| BF16 pattern of the 2n values in `w` (NaN patterns sort above Inf).
 template <int N>
-__device__ __forceinline__ uint32_t max_abs_bits(const uint32_t (&w)[N]) {
-  uint32_t m = 0;
+__device__ __forceinline__ float amax_generic(const uint32_t (&f)[N], float init) {
+  float a = init;
 #pragma unroll
-  for (int i = 0; i < N; ++i) m = vmax_u16x2(m, w[i] & 0x7FFF7FFFu);
+  for (int i = 0; i < N; ++i) a = fmaxf(a, fabsf(__uint_as_float(f[i])));
+  return a;
+}
+
+// ------------------------------------------------------------ fast path
+// Exact scale exponent from the largest finite |x| pattern (see file header).
+__device__ __forceinline__ void scale_fast(uint32_t mb, uint32_t& byte, uint64_t& inv2) {
+  int k = (int)(mb >> 7) - 129 + ((mb & 0x7Fu) > 0x40u ? 1 : 0);
+  k = k < -33 ? -33 : k;
+  byte = (uint32_t)(k + 127);
+  const uint64_t ib = (uint64_t)((uint32_t)(127 - k) << 23);
+  inv2 = (ib << 32) | ib;  // 2^-k in both f32x2 lanes
+}
+
+// 8 values given as float bit patterns times 2^-k -> one code word.
+__device__ __forceinline__ uint32_t encode8_fast(const uint32_t (&f)[8], uint64_t inv2) {
+  uint32_t r;
+  asm("{\n"
+      ".reg .b64 x0, x1, x2, x3;\n"
+      ".reg .f32 a0, b0, a1, b1, a2, b2, a3, b3;\n"
+      ".reg .b8 c0, c1, c2, c3;\n"
+      "mov.b64 x0, {%1, %2};\n"
+      "mov.b64 x1, {%3, %4};\n"
+      "mov.b64 x2, {%5, %6};\n"
+      "mov.b64 x3, {%7, %8};\n"
+      "mul.rn.f32x2 x0, x0, %9;\n"
+      "mul.rn.f32x2 x1, x1, %9;\n"
+      "mul.rn.f32x2 x2, x2, %9;\n"
+      "mul.rn.f32x2 x3, x3, %9;\n"
+      "mov.b64 {a0, b0}, x0;\n"
+      "mov.b64 {a1, b1}, x1;\n"
+      "mov.b64 {a2, b2}, x2;\n"
+      "mov.b64 {a3, b3}, x3;\n"
+      "cvt.rn.satfinite.e2m1x2.f32 c0, b0, a0;\n"
+      "cvt.rn.satfinite.e2m1x2.f32 c1, b1, a1;\n"
+      "cvt.rn.satfinite.e2m1x2.f32 c2, b2, a2;\n"
+      "cvt.rn.satfinite.e2m1x2.f32 c3, b3, a3;\n"
+      "mov.b32 %0, {c0, c1, c2, c3};\n"
+      "}"
+      : "=r"(r)
+      : "r"(f[0]), "r"(f[1]), "r"(f[2]), "r"(f[3]), "r"(f[4]), "r"(f[5]), "r"(f[6]), "r"(f[7]),
+        "l"(inv2));
+  return r;
+}
+
+// Largest |x| BF16 pattern of the BF16 pairs in w; >= 0x7F80 when an Inf or
+// NaN is present (NaN reduces to 0x7FFF).
+template <int N>
+__device__ __forceinline__ uint32_t max_abs_pairs(const uint32_t (&w)[N]) {
+  const uint32_t m = absmax_tree<N>(w) & 0x7FFF7FFFu;
   return max(m & 0xFFFFu, m >> 16);
 }
 
-// Encodes the 2N BF16 values of w (element order) with a known inverse scale
-// into N/2 code words (fast path: |x * inv| <= 6 is guaranteed).
-template <int N>
-__device__ __forceinline__ void encode_fast(const uint32_t (&w)[N], float inv,
-                                            uint32_t (&out)[N / 4]) {
+// Four BF16 pairs (8 consecutive elements) -> their float bit patterns.
+__device__ __forceinline__ void unpack8(const uint32_t* w, uint32_t (&f)[8]) {
 #pragma unroll
-  for (int i = 0; i < N / 4; ++i) {
-    float v[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      v[2 * j] = bf16lo_to_f(w[4 * i + j]) * inv;
-      v[2 * j + 1] = bf16hi_to_f(w[4 * i + j]) * inv;
-    }
-    out[i] = cvt_e2m1x8(v);
+  for (int j = 0; j < 4; ++j) {
+    f[2 * j] = w[j] << 16;
+    f[2 * j + 1] = w[j] & 0xFFFF0000u;
   }
 }
 
-template <int N>
-__device__ __forceinline__ void encode_generic(const uint32_t (&w)[N], float inv,
-                                               const QuantParams& p, uint32_t (&out)[N / 4]) {
+// Quantizes one 32-element block held as 16 BF16 pairs in element order.
+template <bool kFast>
+__device__ __forceinline__ void quant_block32(const uint32_t (&w)[16], const QuantParams& p,
+                                              uint32_t (&out)[4], uint32_t& byte) {
+  const uint32_t mb = max_abs_pairs(w);
+  if (kFast && mb < 0x7F80u) {
+    uint64_t inv2;
+    scale_fast(mb, byte, inv2);
 #pragma unroll
-  for (int i = 0; i < N / 4; ++i) {
-    uint32_t r = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float q0 = fminf(fmaxf(bf16lo_to_f(w[4 * i + j]) * inv, p.fp4_min), p.fp4_max);
-      const float q1 = fminf(fmaxf(bf16hi_to_f(w[4 * i + j]) * inv, p.fp4_min), p.fp4_max);
-      r |= (e2m1_encode_generic(q0) | (e2m1_encode_generic(q1) << 4)) << (8 * j);
+    for (int i = 0; i < 4; ++i) {
+      uint32_t f[8];
+      unpack8(&w[4 * i], f);
+      out[i] = encode8_fast(f, inv2);
     }
-    out[i] = r;
-  }
-}
-
-template <int N>
-__device__ __forceinline__ float amax_generic(const uint32_t (&w)[N], float init) {
-  float a = init;
+  } else {
+    uint32_t fa[32];
 #pragma unroll
-  for (int i = 0; i < N; ++i) {
-    a = fmaxf(a, fabsf(bf16lo_to_f(w[i])));
-    a = fmaxf(a, fabsf(bf16hi_to_f(w[i])));
+    for (int i = 0; i < 4; ++i) {
+      uint32_t f[8];
+      unpack8(&w[4 * i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) fa[8 * i + j] = f[j];
+    }
+    float inv;
+    scale_generic(amax_generic(fa, p.eps), p, inv, byte);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t f[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = fa[8 * i + j];
+      out[i] = encode8_generic(f, inv, p);
+    }
   }
-  return a;
 }
 
 __device__ __forceinline__ int64_t swizzle_offset(int64_t r, int64_t c, int64_t sp4) {
@@ -150,19 +211,28 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __
     const uint8_t* src = reinterpret_cast<const uint8_t*>(x + r * ldx + g * 32 + half * 16);
     const uint4 a = ld_stream_v4(src), b = ld_stream_v4(src + 16);
     const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    uint32_t mb = max_abs_bits(w);
+    uint32_t mb = max_abs_pairs(w);
     mb = max(mb, __shfl_xor_sync(pair_mask, mb, 1));
-    float inv;
-    uint32_t byte;
-    uint32_t out[2];
+    uint32_t byte, out[2];
     if (kFast && mb < 0x7F80u) {
-      scale_fast(mb, p.eps, inv, byte);
-      encode_fast(w, inv, out);
+      uint64_t inv2;
+      scale_fast(mb, byte, inv2);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        uint32_t f[8];
+        unpack8(&w[4 * i], f);
+        out[i] = encode8_fast(f, inv2);
+      }
     } else {
-      float am = amax_generic(w, p.eps);
+      uint32_t f0[8], f1[8];
+      unpack8(&w[0], f0);
+      unpack8(&w[4], f1);
+      float am = fmaxf(amax_generic(f0, p.eps), amax_generic(f1, p.eps));
       am = fmaxf(am, __shfl_xor_sync(pair_mask, am, 1));
+      float inv;
       scale_generic(am, p, inv, byte);
-      encode_generic(w, inv, p, out);
+      out[0] = encode8_generic(f0, inv, p);
+      out[1] = encode8_generic(f1, inv, p);
     }
     st_stream_v2(codes + r * (K >> 1) + g * 16 + half * 8, make_uint2(out[0], out[1]));
     if (half == 0) scales[r * G + g] = (uint8_t)byte;
@@ -170,106 +240,214 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __
 }
 
 // ------------------------------------------------------- fused Q-row + Q-col
-// One CTA quantizes a 128x128 tile: phase 1 reads the tile with 16-byte loads,
-// quantizes its rows from registers and parks the BF16 tile in shared memory;
-// phase 2 quantizes its columns (32-row blocks) from shared memory.  HBM sees
-// every input byte once and every output byte once.
+// Persistent, warp-specialised kernel, two CTAs per SM.  Each CTA walks
+// 128x128 BF16 tiles (tile = blockIdx.x + i * gridDim.x):
+//   * a producer warp streams tiles into a ring of kStages shared-memory
+//     buffers with TMA (one 32 KiB cp.async.bulk.tensor per tile, completion on
+//     full[s]); eight consumer warps release a buffer on empty[s];
+//   * row pass: a thread quantizes two 1x32 row blocks (64 contiguous bytes);
+//     col pass: a thread quantizes a column pair over one 32-row block;
+//   * both passes write their codes into a double-buffered shared-memory
+//     staging area (two 128 x 64-byte boxes, 64-byte TMA swizzle) and their
+//     E8M0 bytes into 128 x 4-byte scale boxes; after one consumer barrier a
+//     single thread writes the two code boxes with TMA stores and every
+//     consumer thread writes one 4-byte scale word.
+// Staging keeps the SM's load/store unit out of the transpose: written
+// directly, the column pass would issue 16-byte stores to 32 rows 8 KiB apart
+// and single-byte scale stores, which bound the kernel well below HBM speed.
+// The input tile is stored densely (256-byte rows); the row pass rotates the
+// order in which a thread reads its four 16-byte chunks by (row % 4) so that
+// the eight lanes of each shared-memory phase hit eight different bank groups.
+// HBM sees every input byte once and every output byte once.
 constexpr int kTile = 128;
-constexpr int kRowColThreads = 256;
+constexpr int kStages = 2;
+constexpr uint32_t kTileBytes = kTile * kTile * 2;  // 32 KiB of BF16
+constexpr uint32_t kCodeBox = kTile * 64;           // 8 KiB: 128 rows x 64 code bytes
+constexpr uint32_t kScaleBox = kTile * 4;           // 128 rows x 4 scale bytes
+constexpr uint32_t kStageOut = 2 * kCodeBox + 2 * kScaleBox;
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kRowColThreads = kConsumers + 32;
+constexpr size_t kRowColSmem = kStages * kTileBytes + 2 * kStageOut + 2 * kStages * 8 + 1024;
+
+// Rotates four words right by r (o[(j + r) & 3] = in[j]) without local memory.
+__device__ __forceinline__ void rotate4(uint32_t (&o)[4], uint32_t r) {
+  uint32_t a[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) a[j] = (r & 1) ? o[(j + 3) & 3] : o[j];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) o[j] = (r & 2) ? a[(j + 2) & 3] : a[j];
+}
+
+// Byte offset of 16-byte chunk `c` of row `r` in a 128 x 64-byte box laid out
+// with the TMA 64-byte swizzle (chunk index XOR bits 7..8 of the offset).
+__device__ __forceinline__ uint32_t sw64(uint32_t r, uint32_t c) {
+  return r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
+}
 
 template <bool kFast, bool kRows>
-__global__ void __launch_bounds__(kRowColThreads) quant_rowcol_kernel(
-    const __nv_bfloat16* __restrict__ x, int64_t M, int64_t K, int64_t ldx,
-    uint8_t* __restrict__ codes_row, uint8_t* __restrict__ scales_row,
-    uint8_t* __restrict__ codes_col, uint8_t* __restrict__ scales_col,
-    uint8_t* __restrict__ scales_swz, QuantParams p) {
-  __shared__ __align__(16) uint32_t tile[kTile][kTile / 2];  // BF16 pairs, 32 KiB
+__global__ void __launch_bounds__(kRowColThreads, 2) quant_rowcol_kernel(
+    const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__ CUtensorMap tmap_row,
+    const __grid_constant__ CUtensorMap tmap_col, int64_t M, int64_t K,
+    uint8_t* __restrict__ scales_row, uint8_t* __restrict__ scales_col,
+    uint8_t* __restrict__ scales_swz, QuantParams p, int col_tiles, int tiles) {
+  extern __shared__ uint8_t smem_raw[];
+  // 1 KiB alignment for the swizzled staging boxes
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* out_base = smem + kStages * kTileBytes;  // 2 x kStageOut
+  uint64_t* full = reinterpret_cast<uint64_t*>(out_base + 2 * kStageOut);
+  uint64_t* empty = full + kStages;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int64_t row0 = (int64_t)blockIdx.y * kTile, col0 = (int64_t)blockIdx.x * kTile;
-  const int64_t G = K >> 5, Gc = M >> 5;
-  const int64_t sp4 = (G + 3) >> 2;
+  const int my_tiles =
+      (int)blockIdx.x < tiles ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int64_t G = K >> 5, Gc = M >> 5, sp4 = (G + 3) >> 2;
 
-  // ---- phase 1: load, row-quantize, stage
-  uint4 v[8];
+  if (t == 0) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int c = i * kRowColThreads + t;
-    const int r = c >> 4, cc = c & 15;
-    const bool ok = (row0 + r < M) && (col0 + cc * 8 < K);
-    v[i] = ok ? ld_stream_v4(x + (row0 + r) * ldx + col0 + cc * 8) : make_uint4(0, 0, 0, 0);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
   }
-  const unsigned quad_mask = 0xFu << (lane & ~3);
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------ producer warp
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < my_tiles; ++i) {
+        const int s = i % kStages;
+        if (i >= kStages && !mbar_wait(&empty[s], (uint32_t)(i / kStages - 1) & 1u)) break;
+        fence_proxy_async_smem();
+        const int tile = (int)blockIdx.x + i * (int)gridDim.x;
+        const int rt = tile / col_tiles, ct = tile - rt * col_tiles;
+        mbar_arrive_expect_tx(&full[s], kTileBytes);
+        tma_load_2d(smem + s * kTileBytes, &tmap_in, ct * kTile, rt * kTile, &full[s]);
+        issued = i + 1;
+      }
+      // do not leave while copies of this CTA are still landing
+      for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
+        mbar_wait(&full[i % kStages], (uint32_t)(i / kStages) & 1u);
+    }
+    return;
+  }
+
+  // -------------------------------------------------- consumer warps
+  bool alive = true;
+  for (int i = 0; i < my_tiles; ++i) {
+    const int s = i % kStages;
+    alive = alive && mbar_wait(&full[s], (uint32_t)(i / kStages) & 1u);
+    const uint8_t* ts = smem + s * kTileBytes;
+    uint8_t* ob = out_base + (i & 1) * kStageOut;
+    uint8_t* o_row = ob;                       // row codes box   [128 rows][64 B]
+    uint8_t* o_col = ob + kCodeBox;            // col codes box   [128 cols][64 B]
+    uint8_t* s_row = ob + 2 * kCodeBox;        // row scales      [128 rows][4]
+    uint8_t* s_col = s_row + kScaleBox;        // col scales      [128 cols][4]
+    const int tile = (int)blockIdx.x + i * (int)gridDim.x;
+    const int rt = tile / col_tiles, ct = tile - rt * col_tiles;
+    const int64_t row0 = (int64_t)rt * kTile, col0 = (int64_t)ct * kTile;
+
+    if (kRows && alive) {
+      const uint32_t rsub = lane & 3, gsel = (lane >> 2) & 1, rhi = lane >> 3;
+      const int r = warp * 16 + (int)(rhi * 4 + rsub);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int c = i * kRowColThreads + t;
-    const int r = c >> 4, cc = c & 15;
-    *reinterpret_cast<uint4*>(&tile[r][cc * 4]) = v[i];
-    if (kRows) {
-      const bool ok = (row0 + r < M) && (col0 + cc * 8 < K);  // uniform per quad
-      if (ok) {
-        const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-        uint32_t mb = max_abs_bits(w);
-        mb = max(mb, __shfl_xor_sync(quad_mask, mb, 1));
-        mb = max(mb, __shfl_xor_sync(quad_mask, mb, 2));
-        float inv;
-        uint32_t byte;
-        uint32_t out[1];
-        if (kFast && mb < 0x7F80u) {
-          scale_fast(mb, p.eps, inv, byte);
-          encode_fast(w, inv, out);
-        } else {
-          float am = amax_generic(w, p.eps);
-          am = fmaxf(am, __shfl_xor_sync(quad_mask, am, 1));
-          am = fmaxf(am, __shfl_xor_sync(quad_mask, am, 2));
-          scale_generic(am, p, inv, byte);
-          encode_generic(w, inv, p, out);
+      for (int k = 0; k < 2; ++k) {
+        const int g = 2 * k + (int)gsel;
+        uint32_t w[16];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t c = (j + rsub) & 3;
+          const uint4 v = *reinterpret_cast<const uint4*>(ts + r * 256 + g * 64 + c * 16);
+          w[4 * j] = v.x; w[4 * j + 1] = v.y; w[4 * j + 2] = v.z; w[4 * j + 3] = v.w;
         }
-        const int64_t gr = row0 + r, gc = col0 + cc * 8;
-        st_stream_u32(codes_row + gr * (K >> 1) + (gc >> 1), out[0]);
-        if ((cc & 3) == 0) {
-          const int64_t g = gc >> 5;
-          scales_row[gr * G + g] = (uint8_t)byte;
-          if (scales_swz) scales_swz[swizzle_offset(gr, g, sp4)] = (uint8_t)byte;
+        uint32_t out[4], byte;
+        quant_block32<kFast>(w, p, out, byte);  // out[j] encodes chunk (j + rsub) & 3
+        rotate4(out, rsub);
+        *reinterpret_cast<uint4*>(o_row + sw64(r, g)) = make_uint4(out[0], out[1], out[2], out[3]);
+        s_row[r * 4 + g] = (uint8_t)byte;
+        if (scales_swz) {
+          const int64_t gr = row0 + r, gg = (col0 >> 5) + g;
+          if (gr < M && gg < G) scales_swz[swizzle_offset(gr, gg, sp4)] = (uint8_t)byte;
+        }
+      }
+    }
+
+    if (alive) {
+      const int cp = ((warp & 1) << 5) | lane;  // column pair within the tile
+      const int rb = warp >> 1;                 // 32-row block within the tile
+      uint32_t w[32];  // rows rb*32 .. +31, columns (2cp, 2cp + 1) as BF16 pairs
+#pragma unroll
+      for (int r = 0; r < 32; ++r)
+        w[r] = *reinterpret_cast<const uint32_t*>(ts + (rb * 32 + r) * 256 + cp * 4);
+      const uint32_t m = absmax_tree<32>(w) & 0x7FFF7FFFu;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t mb = h ? (m >> 16) : (m & 0xFFFFu);
+        uint32_t out[4], byte;
+        if (kFast && mb < 0x7F80u) {
+          uint64_t inv2;
+          scale_fast(mb, byte, inv2);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t f[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              f[j] = h ? (w[8 * q + j] & 0xFFFF0000u) : (w[8 * q + j] << 16);
+            out[q] = encode8_fast(f, inv2);
+          }
+        } else {
+          uint32_t fa[32];
+#pragma unroll
+          for (int r = 0; r < 32; ++r) fa[r] = h ? (w[r] & 0xFFFF0000u) : (w[r] << 16);
+          float inv;
+          scale_generic(amax_generic(fa, p.eps), p, inv, byte);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t f[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] = fa[8 * q + j];
+            out[q] = encode8_generic(f, inv, p);
+          }
+        }
+        const int c = 2 * cp + h;
+        *reinterpret_cast<uint4*>(o_col + sw64(c, rb)) = make_uint4(out[0], out[1], out[2], out[3]);
+        s_col[c * 4 + rb] = (uint8_t)byte;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with input stage s
+    fence_proxy_async_smem();               // staging writes -> visible to the TMA store
+    if (t == 0) bulk_wait_read_all();       // the previous tile's stores have read their box
+    if (named_sync_or(1, kConsumers, !alive)) break;  // a tile never arrived: stop together
+    if (t == 0) {
+      if (kRows) tma_store_2d(&tmap_row, (int32_t)(col0 >> 1), (int32_t)row0, o_row);
+      tma_store_2d(&tmap_col, (int32_t)(row0 >> 1), (int32_t)col0, o_col);
+      bulk_commit();
+    }
+    // scale words: thread t < 128 -> row scales of row t; t >= 128 -> col scales of column t-128
+    {
+      const bool is_row = t < kTile;
+      if (is_row && !kRows) continue;
+      const int idx = is_row ? t : t - kTile;
+      const int64_t lim_outer = is_row ? M : K, lim_inner = is_row ? G : Gc;
+      const int64_t outer = (is_row ? row0 : col0) + idx;
+      const int64_t inner0 = (is_row ? col0 : row0) >> 5;
+      uint8_t* dst_base = is_row ? scales_row : scales_col;
+      const uint32_t word = *reinterpret_cast<const uint32_t*>((is_row ? s_row : s_col) + idx * 4);
+      if (outer < lim_outer) {
+        uint8_t* dst = dst_base + outer * lim_inner + inner0;
+        const int64_t n = min((int64_t)4, lim_inner - inner0);
+        if (n == 4 && (reinterpret_cast<uintptr_t>(dst) & 3) == 0) {
+          *reinterpret_cast<uint32_t*>(dst) = word;
+        } else {
+          for (int j = 0; j < n; ++j) dst[j] = (uint8_t)(word >> (8 * j));
         }
       }
     }
   }
-  __syncthreads();
-
-  // ---- phase 2: column-quantize 32-row blocks from shared memory
-  const int rb = warp >> 1;                 // 32-row block of the tile
-  const int cp = ((warp & 1) << 5) | lane;  // column pair within the tile
-  const int64_t gc = col0 + 2 * cp;
-  const int64_t gr = row0 + rb * 32;
-  if (gr >= M || gc >= K) return;
-  uint32_t w[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) w[i] = tile[rb * 32 + i][cp];
-  uint32_t m = 0;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) m = vmax_u16x2(m, w[i] & 0x7FFF7FFFu);
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const uint32_t mb = h ? (m >> 16) : (m & 0xFFFFu);
-    // the 32 values of column gc + h, as BF16 pairs (rows 2i, 2i+1)
-    uint32_t cw[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-      cw[i] = h ? prmt(w[2 * i], w[2 * i + 1], 0x7632u) : prmt(w[2 * i], w[2 * i + 1], 0x5410u);
-    float inv;
-    uint32_t byte;
-    uint32_t out[4];
-    if (kFast && mb < 0x7F80u) {
-      scale_fast(mb, p.eps, inv, byte);
-      encode_fast(cw, inv, out);
-    } else {
-      scale_generic(amax_generic(cw, p.eps), p, inv, byte);
-      encode_generic(cw, inv, p, out);
-    }
-    const int64_t c = gc + h;
-    st_stream_v4(codes_col + c * (M >> 1) + (gr >> 1), make_uint4(out[0], out[1], out[2], out[3]));
-    scales_col[c * Gc + (gr >> 5)] = (uint8_t)byte;
-  }
+  if (t == 0) bulk_wait_all();
 }
 
 __global__ void swizzle_scales_kernel(const uint8_t* __restrict__ s, int64_t M, int64_t S,
@@ -344,8 +522,8 @@ extern "C" mxb_status mxb_quant_mxfp4_rowcol(const void* input, int64_t M, int64
   if (M == 0 || K == 0) return MXB_OK;
   MXB_REQUIRE(input && codes_col && scales_col, MXB_ERR_INVALID_ARGUMENT,
               "quant_rowcol: null pointer");
-  MXB_REQUIRE(aligned(input, 16) && aligned(codes_col, 16) && (!codes_row || aligned(codes_row, 4)),
-              MXB_ERR_MISALIGNED, "quant_rowcol: input/codes_col must be 16-byte aligned");
+  MXB_REQUIRE(aligned(input, 16) && aligned(codes_col, 16) && (!codes_row || aligned(codes_row, 16)),
+              MXB_ERR_MISALIGNED, "quant_rowcol: input and code outputs must be 16-byte aligned");
   cudaStream_t s = to_cuda(stream);
   if (scales_row_swizzled) {
     const int64_t bytes = (M + 127) / 128 * 128 * ((K / 32 + 3) / 4 * 4);
@@ -355,25 +533,48 @@ extern "C" mxb_status mxb_quant_mxfp4_rowcol(const void* input, int64_t M, int64
   }
   const QuantParams p{eps, fp4_min, fp4_max};
   const bool fast = fast_params(eps, fp4_min, fp4_max);
-  const dim3 grid((unsigned)cdiv(K, kTile), (unsigned)cdiv(M, kTile));
-  auto* xi = (const __nv_bfloat16*)input;
-  auto* cr = (uint8_t*)codes_row;
+  CUtensorMap tm_in, tm_row, tm_col;
+  if (!make_tensor_map_2d(&tm_in, input, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, ldx, kTile,
+                          kTile))
+    return MXB_ERR_CUDA;
+  // code outputs: uint8 [M, K/2] and [K, M/2], 64-byte x 128-row boxes, 64-byte swizzle
+  if (codes_row && !make_tensor_map_2d(&tm_row, codes_row, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M,
+                                       K / 2, K / 2, 64, kTile, CU_TENSOR_MAP_SWIZZLE_64B))
+    return MXB_ERR_CUDA;
+  if (!codes_row) tm_row = tm_in;  // unused when the row outputs are skipped
+  if (!make_tensor_map_2d(&tm_col, codes_col, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M / 2, M / 2,
+                          64, kTile, CU_TENSOR_MAP_SWIZZLE_64B))
+    return MXB_ERR_CUDA;
+  const int64_t col_tiles = cdiv(K, kTile), tiles = col_tiles * cdiv(M, kTile);
+  MXB_REQUIRE(tiles < (1LL << 31), MXB_ERR_INVALID_ARGUMENT, "quant_rowcol: tensor too large");
   auto* sr = (uint8_t*)scales_row;
-  auto* cc = (uint8_t*)codes_col;
   auto* sc = (uint8_t*)scales_col;
   auto* sw = (uint8_t*)scales_row_swizzled;
-  if (codes_row) {
-    if (fast)
-      quant_rowcol_kernel<true, true><<<grid, kRowColThreads, 0, s>>>(xi, M, K, ldx, cr, sr, cc, sc, sw, p);
-    else
-      quant_rowcol_kernel<false, true><<<grid, kRowColThreads, 0, s>>>(xi, M, K, ldx, cr, sr, cc, sc, sw, p);
-  } else {
-    if (fast)
-      quant_rowcol_kernel<true, false><<<grid, kRowColThreads, 0, s>>>(xi, M, K, ldx, cr, sr, cc, sc, sw, p);
-    else
-      quant_rowcol_kernel<false, false><<<grid, kRowColThreads, 0, s>>>(xi, M, K, ldx, cr, sr, cc, sc, sw, p);
-  }
+  using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, int64_t, int64_t,
+                        uint8_t*, uint8_t*, uint8_t*, QuantParams, int, int);
+  Kern kern = codes_row ? (fast ? quant_rowcol_kernel<true, true> : quant_rowcol_kernel<false, true>)
+                        : (fast ? quant_rowcol_kernel<true, false> : quant_rowcol_kernel<false, false>);
+  static const bool attr_ok = [] {
+    bool ok = true;
+    for (Kern k : {quant_rowcol_kernel<true, true>, quant_rowcol_kernel<false, true>,
+                   quant_rowcol_kernel<true, false>, quant_rowcol_kernel<false, false>})
+      ok &= cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kRowColSmem) == cudaSuccess;
+    return ok;
+  }();
+  MXB_REQUIRE(attr_ok, MXB_ERR_CUDA, "quant_rowcol: cannot reserve %zu bytes of shared memory",
+              kRowColSmem);
+  const int64_t cap = (int64_t)persistent_ctas((const void*)kern, kRowColThreads, kRowColSmem);
+  const int grid = (int)(tiles < cap ? tiles : cap);
+  kern<<<grid, kRowColThreads, kRowColSmem, s>>>(tm_in, tm_row, tm_col, M, K, sr, sc, sw, p,
+                                                 (int)col_tiles, (int)tiles);
   return launch_status("quant_rowcol");
+}
+
+extern "C" unsigned int mxb_wait_timeouts(void) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_mxb_wait_timeouts, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  return v;
 }
 
 extern "C" mxb_status mxb_swizzle_scales(const void* scales, int64_t M, int64_t S, void* out,

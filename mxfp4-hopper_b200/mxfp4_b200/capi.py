@@ -61,6 +61,7 @@ def load() -> ctypes.CDLL:
             fn.restype = ctypes.c_int
         L.mxb_last_error.restype = ctypes.c_char_p
         L.mxb_version.restype = ctypes.c_char_p
+        L.mxb_wait_timeouts.restype = ctypes.c_uint
         _lib = L
     return _lib
 
@@ -80,6 +81,10 @@ def status_of(name: str, *args) -> int:
 
 def last_error() -> str:
     return load().mxb_last_error().decode()
+
+
+def wait_timeouts() -> int:
+    return int(load().mxb_wait_timeouts())
 
 
 def version() -> str:
