@@ -129,6 +129,17 @@ __device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
   return r;
 }
 
+// (a, b) * s for two floats given as bit patterns, one mul.rn.f32x2.
+__device__ __forceinline__ void mul2_f32(uint32_t a, uint32_t b, float s, float& ra, float& rb) {
+  asm("{\n .reg .b64 x, y;\n"
+      " mov.b64 x, {%2, %3};\n"
+      " mov.b64 y, {%4, %4};\n"
+      " mul.rn.f32x2 x, x, y;\n"
+      " mov.b64 {%0, %1}, x;\n}"
+      : "=f"(ra), "=f"(rb)
+      : "r"(a), "r"(b), "f"(s));
+}
+
 // ---------------------------------------------------------------- E2M1 decode
 // BF16 bit patterns of the eight E2M1 magnitudes {0,.5,1,1.5,2,3,4,6}, split
 // into byte tables so that `prmt` can look up four nibbles at once.

@@ -1,24 +1,33 @@
 // MXFP4 (rowwise) -> transposed FP8 E4M3 converts for sm_100a: the
 // columnwise GEMM operands of the reference.
 //
-//  * col      (code/kernel/per_token_Mxfp4ToFp8_col.cu:110-301): scale per
+//  * col        (code/kernel/per_token_Mxfp4ToFp8_col.cu:110-301): scale per
 //    (128-row block, 32-column block) from the largest E8M0 exponent; 8-bit
-//    exponent re-basing with the sign bit masked off.
-//  * colT     (per_token_Mxfp4RowToBf16ToFp8Col.cu:42-197): true-amax scale
-//    per (128-row block, column), amax/448 stored.
+//    exponent re-basing with the sign bit masked off (table in fp8_lut.cuh).
+//  * colT       (per_token_Mxfp4RowToBf16ToFp8Col.cu:42-197): true-amax scale
+//    per (128-row block, column), amax/448 stored; race-free.
 //  * colT-split (per_token_Mxfp4RowToBf16ToFp8Col_msplit.cu:51-224): the same
 //    per m_split segment with power-of-two scales (1/scale stored) and a
 //    contiguous [N, m_i] output block per segment.
 //
-// All three read a 128-row tile of codes once with 16-byte loads, transpose
-// through shared memory and write whole 16-byte runs of the [N, M] output.
+// Each CTA owns one 128-row x 64-code-byte tile.  One TMA load brings the
+// codes into shared memory with the 64-byte swizzle, so that a warp whose
+// lanes are 32 consecutive rows reads them without bank conflicts.  Results
+// are transposed through shared memory and leave as 128-byte runs of output
+// rows, eight lanes per run.  Several CTAs per SM overlap one tile's load
+// with the others' work.
 #include "capi_util.h"
 #include "common.cuh"
+#include "fp8_lut.cuh"
+#include "tma.cuh"
 
 namespace mxb {
 namespace {
 
 constexpr int kThreads = 256;
+constexpr uint32_t kCodeTileBytes = 128 * 64;
+
+__device__ const Fp8Lut g_lut_col = make_fp8_lut(true);
 
 __device__ __forceinline__ uint32_t vmax_u8x4(uint32_t a, uint32_t b) {
   uint32_t r;
@@ -26,64 +35,89 @@ __device__ __forceinline__ uint32_t vmax_u8x4(uint32_t a, uint32_t b) {
   return r;
 }
 
-// ------------------------------------------------------------------ col (C4)
-// Tile: 128 rows x 64 code bytes (128 elements, four 32-column scale blocks).
-constexpr int kColPitch = 144;  // bytes per transposed row in shared memory
+// 16-byte chunk c of row r of a 128 x 64-byte tile loaded with the TMA
+// 64-byte swizzle (chunk index XOR bits 7..8 of the byte offset).
+__device__ __forceinline__ uint4 ld_code_chunk(const uint8_t* tile, int r, int c) {
+  return *reinterpret_cast<const uint4*>(tile + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+}
 
-__global__ void __launch_bounds__(kThreads) fp8_col_kernel(const uint8_t* __restrict__ codes,
+// Loads the tile with one TMA and waits (bounded).  Returns false, for every
+// thread of the CTA, if the copy never completed.
+__device__ __forceinline__ bool load_code_tile(uint8_t* tile, uint64_t* bar, const CUtensorMap* map,
+                                               int32_t x, int32_t y) {
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(bar, kCodeTileBytes);
+    tma_load_2d(tile, map, x, y, bar);
+  }
+  const bool ok = mbar_wait(bar, 0);
+  return !__syncthreads_or(!ok);
+}
+
+// ------------------------------------------------------------------ col (C4)
+// Lane = row.  A lane turns its row's 16-byte code chunk into eight words of
+// four FP8 bytes (elements 4k..4k+3 of that row); four neighbouring lanes then
+// transpose their 4x4 byte blocks with two shuffles so that each lane holds
+// four rows of one element and stores them as one word of the transposed tile.
+constexpr int kColPitch = 160;  // bytes per element row of the transposed tile
+
+// 4x4 byte transpose across lanes 4m..4m+3: in, lane i holds row i's bytes for
+// elements 0..3; out, lane i holds element i's bytes for rows 0..3.
+__device__ __forceinline__ uint32_t transpose4x4(uint32_t w, uint32_t lane) {
+  const uint32_t b1 = lane & 1u, b2 = lane & 2u;
+  uint32_t o = __shfl_xor_sync(0xffffffffu, w, 2);
+  uint32_t t = b2 ? prmt(o, w, 0x7632u) : prmt(w, o, 0x5410u);
+  o = __shfl_xor_sync(0xffffffffu, t, 1);
+  return b1 ? prmt(o, t, 0x7351u) : prmt(t, o, 0x6240u);
+}
+
+__global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant__ CUtensorMap tmap,
                                                            const uint8_t* __restrict__ scales,
                                                            int64_t M, int64_t Kb,
                                                            uint8_t* __restrict__ out,
                                                            float* __restrict__ scales_out) {
+  __shared__ __align__(1024) uint8_t ctile[kCodeTileBytes];
   __shared__ __align__(16) uint8_t tr[128 * kColPitch];  // [element][row] FP8
-  __shared__ uint32_t sc_row[128];                        // 4 E8M0 bytes per row
   __shared__ uint32_t red[4];
+  __shared__ uint64_t bar;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int rb = warp >> 1, hh = warp & 1;  // 32-row block, 32-byte half of the tile
   const int64_t row0 = (int64_t)blockIdx.y * 128;
   const int64_t cb0 = (int64_t)blockIdx.x * 64;  // first code byte of the tile
   const int64_t S = Kb / 16;
+  const int r = rb * 32 + lane;
 
-  if (t < 128) {
-    const uint32_t s = ld_stream_u32(scales + (row0 + t) * S + cb0 / 16);
-    sc_row[t] = s;
-    uint32_t m = s;
+  // this row's four E8M0 bytes (one per 32-column block of the tile)
+  const uint32_t sc = ld_stream_u32(scales + (row0 + r) * S + cb0 / 16);
+  if (hh == 0) {
+    uint32_t m = sc;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = vmax_u8x4(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[warp] = m;
+    if (lane == 0) red[rb] = m;
   }
-  // codes: 512 chunks of 16 bytes; chunk i -> (scale column q = i / 128, row i % 128)
-  uint4 v[2];
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int i = k * kThreads + t;
-    v[k] = ld_stream_v4(codes + (row0 + (i & 127)) * Kb + cb0 + (i >> 7) * 16);
-  }
-  __syncthreads();
+  if (!load_code_tile(ctile, &bar, &tmap, (int32_t)cb0, (int32_t)row0)) return;
   const uint32_t mx = vmax_u8x4(vmax_u8x4(red[0], red[1]), vmax_u8x4(red[2], red[3]));
+  // this lane stores element (4k + (lane & 3)) for rows (lane & ~3) .. +3
+  uint8_t* trl = tr + (lane & 3) * kColPitch + rb * 32 + (lane & ~3);
+
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int i = k * kThreads + t;
-    const int r = i & 127, q = i >> 7;
-    const uint32_t wa = ((mx >> (8 * q)) - 6u) & 0xFFu;
-    const uint32_t e = (sc_row[r] >> (8 * q)) & 0xFFu;
-    const uint32_t adj = (wa - e) & 0xFFu;
-    const uint32_t off16 = (adj << 7) << 16;
-    const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+  for (int cc = 0; cc < 2; ++cc) {
+    const int q = 2 * hh + cc;  // 32-column block
+    const uint4 v = ld_code_chunk(ctile, r, q);
+    const uint32_t d = ((mx >> (8 * q)) & 0xFFu) - ((sc >> (8 * q)) & 0xFFu);
+    const uint2 tb = __ldg(reinterpret_cast<const uint2*>(g_lut_col.v[d]));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      uint32_t x[4];
-      e2m1x4_to_bf16x4(w[j], x[0], x[1]);
-      e2m1x4_to_bf16x4(w[j] >> 16, x[2], x[3]);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float lo = __uint_as_float(((x[u] << 16) - off16) & 0x7FFF0000u);
-        float hi = __uint_as_float(((x[u] & 0xFFFF0000u) - off16) & 0x7FFF0000u);
-        lo = fminf(fmaxf(lo, -448.0f), 448.0f);
-        hi = fminf(fmaxf(hi, -448.0f), 448.0f);
-        const uint32_t b2 = cvt_e4m3x2(lo, hi);
-        const int n = q * 32 + j * 8 + u * 2;
-        tr[n * kColPitch + r] = (uint8_t)b2;
-        tr[(n + 1) * kColPitch + r] = (uint8_t)(b2 >> 8);
+      for (int hw = 0; hw < 2; ++hw) {
+        const uint32_t f4 = lut_lookup4_nosign(w[j] >> (16 * hw), tb.x, tb.y);
+        const int n = q * 32 + j * 8 + hw * 4;
+        *reinterpret_cast<uint32_t*>(trl + n * kColPitch) = transpose4x4(f4, (uint32_t)lane);
       }
     }
   }
@@ -93,20 +127,23 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const uint8_t* __rest
     const uint32_t wa = ((mx >> (8 * (t >> 5))) - 6u) & 0xFFu;
     scales_out[(row0 / 128) * (2 * Kb) + 2 * cb0 + t] = __uint_as_float(wa << 23);
   }
-  // output rows n = 2*cb0 + 0..127, 128 FP8 bytes each at columns row0..row0+127
+  // output rows n = 2*cb0 + 0..127: 128 FP8 bytes each at columns row0..row0+127
+  uint8_t* ob = out + 2 * cb0 * M + row0;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int i = k * kThreads + t;
     const int n = i >> 3, part = i & 7;
     const uint4 o = *reinterpret_cast<const uint4*>(&tr[n * kColPitch + part * 16]);
-    st_stream_v4(out + (2 * cb0 + n) * M + row0 + part * 16, o);
+    st_stream_v4(ob + n * M + part * 16, o);
   }
 }
 
 // ------------------------------------------------------- colT / colT-split
-// Tile: 128 rows x 128 elements (64 code bytes per row).  Phase 1 decodes the
-// tile to BF16 (code x E8M0 scale; exact) in shared memory, phase 2 finds each
-// column's amax, phase 3 scales, clamps and converts columns to FP8.
+// Tile: 128 rows x 128 elements.  Phase 1 decodes the tile to BF16 (code x
+// E8M0 scale, exact) in shared memory, phase 2 finds each column's amax,
+// phase 3 scales, clamps and converts column pairs to FP8 into a transposed
+// staging tile (128-byte rows, 16-byte chunks XOR-swizzled by row / 2), and
+// phase 4 writes that tile out as 128-byte row runs.
 constexpr int kTPitch = 272;  // bytes per BF16 row in shared memory (256 + 16)
 
 struct SplitArgs {
@@ -115,17 +152,26 @@ struct SplitArgs {
   const int32_t* scale_offsets;
 };
 
+__device__ __forceinline__ int out_swz(int n, int chunk) { return n * 128 + ((chunk ^ ((n >> 1) & 7)) << 4); }
+
 template <bool kSplit>
-__global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const uint8_t* __restrict__ codes,
+__global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constant__ CUtensorMap tmap,
                                                             const uint8_t* __restrict__ scales,
                                                             int64_t M, int64_t N, float eps,
                                                             uint8_t* __restrict__ out,
                                                             float* __restrict__ scales_out,
                                                             SplitArgs sa) {
-  __shared__ __align__(16) uint8_t tile[128 * kTPitch];
-  __shared__ uint32_t part_max[4][128];
-  __shared__ float col_qs[128];
-  __shared__ int has_special;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* ctile = smem;                                // 8 KiB codes (64-byte swizzle)
+  uint8_t* tile = smem + kCodeTileBytes;                // 128 x 272 B BF16
+  uint8_t* otile = tile + 128 * kTPitch;                // 128 x 128 B FP8 (swizzled)
+  uint32_t* part_max = reinterpret_cast<uint32_t*>(otile + 128 * 128);  // [4][128]
+  float* col_qs = reinterpret_cast<float*>(part_max + 4 * 128);         // [128]
+  uint32_t* col_clamp = reinterpret_cast<uint32_t*>(col_qs + 128);       // [128]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(col_clamp + 128);
+  int* has_special = reinterpret_cast<int*>(bar + 1);
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
 
   // tile geometry
@@ -150,20 +196,32 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const uint8_t* __res
   }
   const int64_t col0 = (int64_t)blockIdx.z * 128;
   const int64_t cols = min((int64_t)128, N - col0);
-  const int64_t Kb = N / 2, S = N / 32;
-  if (t == 0) has_special = 0;
-  __syncthreads();
+  const int64_t S = N / 32;
+  if (t == 0) *has_special = 0;
 
-  // ---- phase 1: decode (row r, 32-element block q) per chunk
+  // this thread's row (phase 1): lane = row within a 32-row block, warp pair = half
+  const int rb = warp >> 1, hh = warp & 1, r = rb * 32 + lane;
+  uint32_t sc = 0;
+  if (r < rows) {
+    const uint8_t* sp = scales + (row_start + r) * S + col0 / 32;
+    if (cols == 128 && (reinterpret_cast<uintptr_t>(sp) & 3) == 0) {
+      sc = ld_stream_u32(sp);  // the tile's four E8M0 bytes of this row at once
+    } else {
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int i = k * kThreads + t;
-    const int r = i & 127, q = i >> 7;
+      for (int q = 0; q < 4; ++q)
+        if (q * 32 < cols) sc |= (uint32_t)ld_stream_u8(sp + q) << (8 * q);
+    }
+  }
+  if (!load_code_tile(ctile, bar, &tmap, (int32_t)(col0 / 2), (int32_t)row_start)) return;
+
+  // ---- phase 1: decode two 32-element blocks of row r
+#pragma unroll
+  for (int cc = 0; cc < 2; ++cc) {
+    const int q = 2 * hh + cc;
     uint32_t o[16];
     if (r < rows && q * 32 < cols) {
-      const int64_t gr = row_start + r;
-      const uint4 c = ld_stream_v4(codes + gr * Kb + col0 / 2 + q * 16);
-      const uint32_t e = ld_stream_u8(scales + gr * S + col0 / 32 + q);
+      const uint4 c = ld_code_chunk(ctile, r, q);
+      const uint32_t e = (sc >> (8 * q)) & 0xFFu;
       const uint32_t w[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -180,13 +238,13 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const uint8_t* __res
 #pragma unroll
         for (int j = 0; j < 16; ++j)
           o[j] = cvt_bf16x2(bf16lo_to_f(o[j]) * s, bf16hi_to_f(o[j]) * s);
-        if (e == 255u) has_special = 1;
+        if (e == 255u) *has_special = 1;
       }
     } else {
 #pragma unroll
       for (int j = 0; j < 16; ++j) o[j] = 0u;
     }
-    uint4* dst = reinterpret_cast<uint4*>(&tile[r * kTPitch + q * 64]);
+    uint4* dst = reinterpret_cast<uint4*>(tile + r * kTPitch + q * 64);
 #pragma unroll
     for (int j = 0; j < 4; ++j) dst[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
   }
@@ -195,30 +253,30 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const uint8_t* __res
   // ---- phase 2: column amax (thread = column pair x 32-row quarter)
   {
     const int cp = ((warp & 1) << 5) | lane, rq = warp >> 1;
-    const bool special = has_special != 0;
-    if (!special) {
-      uint32_t m = 0;
-#pragma unroll 8
-      for (int i = 0; i < 32; ++i)
-        m = vmax_u16x2(m, *reinterpret_cast<const uint32_t*>(&tile[(rq * 32 + i) * kTPitch + cp * 4]) &
-                              0x7FFF7FFFu);
-      part_max[rq][2 * cp] = (m & 0xFFFFu) << 16;
-      part_max[rq][2 * cp + 1] = m & 0xFFFF0000u;
+    const uint32_t* col = reinterpret_cast<const uint32_t*>(tile + rq * 32 * kTPitch) + cp;
+    if (*has_special == 0) {
+      uint32_t w[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) w[i] = col[i * (kTPitch / 4)];
+      const uint32_t m = absmax_tree<32>(w) & 0x7FFF7FFFu;
+      part_max[rq * 128 + 2 * cp] = (m & 0xFFFFu) << 16;
+      part_max[rq * 128 + 2 * cp + 1] = m & 0xFFFF0000u;
     } else {
       float a0 = 0.0f, a1 = 0.0f;  // fmaxf ignores NaN, as the reference's loop does
       for (int i = 0; i < 32; ++i) {
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(&tile[(rq * 32 + i) * kTPitch + cp * 4]);
+        const uint32_t w = col[i * (kTPitch / 4)];
         a0 = fmaxf(a0, fabsf(bf16lo_to_f(w)));
         a1 = fmaxf(a1, fabsf(bf16hi_to_f(w)));
       }
-      part_max[rq][2 * cp] = __float_as_uint(a0);
-      part_max[rq][2 * cp + 1] = __float_as_uint(a1);
+      part_max[rq * 128 + 2 * cp] = __float_as_uint(a0);
+      part_max[rq * 128 + 2 * cp + 1] = __float_as_uint(a1);
     }
   }
   __syncthreads();
   if (t < 128) {
     // magnitudes are non-negative floats, so integer order is float order
-    const uint32_t mb = max(max(part_max[0][t], part_max[1][t]), max(part_max[2][t], part_max[3][t]));
+    const uint32_t mb = max(max(part_max[t], part_max[128 + t]),
+                            max(part_max[256 + t], part_max[384 + t]));
     const float mxv = __uint_as_float(mb);
     float qs;
     if (!kSplit) {
@@ -227,54 +285,95 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const uint8_t* __res
       qs = (amax > 1e-9f) ? (448.0f / amax) : 0.0f;
     } else {
       const float amax = mxv;  // initialised to 0 on the split path
-      float sc;
+      float s;
       if (amax <= eps) {
-        sc = 1.0f;
+        s = 1.0f;
       } else {
-        const uint32_t rb = __float_as_uint(amax / 448.0f);
-        uint32_t ex = (rb >> 23) & 0xFFu;
-        if (rb & 0x7FFFFFu) ex += 1u;
-        sc = (float)(1.0 / (double)__uint_as_float(ex << 23));
+        const uint32_t rbits = __float_as_uint(amax / 448.0f);
+        uint32_t ex = (rbits >> 23) & 0xFFu;
+        if (rbits & 0x7FFFFFu) ex += 1u;
+        s = (float)(1.0 / (double)__uint_as_float(ex << 23));
       }
-      if (t < cols) scales_out[scale_row * N + col0 + t] = 1.0f / sc;
-      qs = sc;
+      if (t < cols) scales_out[scale_row * N + col0 + t] = 1.0f / s;
+      qs = s;
     }
     col_qs[t] = qs;
+    // NaN products are possible only with an Inf amax or an E8M0 byte of 255
+    col_clamp[t] = (mb >= 0x7F800000u || *has_special) ? 1u : 0u;
   }
   __syncthreads();
 
-  // ---- phase 3: quantize columns; lane -> column, 16-row chunk per task
+  // ---- phase 3: column pair x 16-row chunk -> two 16-byte runs of the staging tile.
+  // With a finite amax every |v * qs| is at most 448 (1 + 2^-23), which the
+  // saturating conversion maps exactly as clamp-then-convert does (true for
+  // every finite value), so the clamp is applied only where a NaN can occur:
+  // columns with an Inf amax (v * 0) and tiles holding an E8M0 byte of 255
+  // (0 * Inf); the reference clamps NaN to -448.
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int n = ((warp & 3) << 5) | lane;
-    const int chunk = (warp >> 2) + 2 * k;  // 0..7
-    if (n >= cols || chunk * 16 >= rows) continue;
-    const float qs = col_qs[n];
-    uint32_t o[4];
+  for (int k = 0; k < 2; ++k) {
+    const int cp = ((warp & 1) << 5) | lane;
+    const int chunk = (warp >> 1) + 4 * k;  // 0..7
+    const uint32_t* col = reinterpret_cast<const uint32_t*>(tile + chunk * 16 * kTPitch) + cp;
+    uint32_t w[16];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint32_t word = 0;
+    for (int i = 0; i < 16; ++i) w[i] = col[i * (kTPitch / 4)];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int r = chunk * 16 + j * 4 + u * 2;
-        const uint32_t b0 = *reinterpret_cast<const uint16_t*>(&tile[r * kTPitch + n * 2]);
-        const uint32_t b1 = *reinterpret_cast<const uint16_t*>(&tile[(r + 1) * kTPitch + n * 2]);
-        float q0 = __uint_as_float(b0 << 16) * qs;
-        float q1 = __uint_as_float(b1 << 16) * qs;
-        q0 = fminf(fmaxf(q0, -448.0f), 448.0f);
-        q1 = fminf(fmaxf(q1, -448.0f), 448.0f);
-        word |= cvt_e4m3x2(q0, q1) << (16 * u);
+    for (int h = 0; h < 2; ++h) {
+      const float qs = col_qs[2 * cp + h];
+      const bool clamp = col_clamp[2 * cp + h] != 0;
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const uint32_t b0 = w[4 * j + 2 * u], b1 = w[4 * j + 2 * u + 1];
+          float q0, q1;
+          mul2_f32(h ? (b0 & 0xFFFF0000u) : (b0 << 16), h ? (b1 & 0xFFFF0000u) : (b1 << 16), qs,
+                   q0, q1);
+          if (clamp) {
+            q0 = fminf(fmaxf(q0, -448.0f), 448.0f);
+            q1 = fminf(fmaxf(q1, -448.0f), 448.0f);
+          }
+          word |= cvt_e4m3x2(q0, q1) << (16 * u);
+        }
+        o[j] = word;
       }
-      o[j] = word;
-    }
-    uint8_t* dst = out + out_base + (col0 + n) * out_pitch + chunk * 16;
-    const int valid = (int)min((int64_t)16, rows - chunk * 16);
-    if (valid == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-      st_stream_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
-    } else {
-      for (int j = 0; j < valid; ++j) dst[j] = (uint8_t)(o[j >> 2] >> (8 * (j & 3)));
+      *reinterpret_cast<uint4*>(otile + out_swz(2 * cp + h, chunk)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
+  __syncthreads();
+
+  // ---- phase 4: output rows n (128 FP8 bytes each), eight lanes per row
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = k * kThreads + t;
+    const int n = i >> 3, part = i & 7;
+    if (n >= cols || part * 16 >= rows) continue;
+    const uint4 o = *reinterpret_cast<const uint4*>(otile + out_swz(n, part));
+    uint8_t* dst = out + out_base + (col0 + n) * out_pitch + part * 16;
+    const int valid = (int)min((int64_t)16, rows - part * 16);
+    if (valid == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+      st_stream_v4(dst, o);
+    } else {
+      const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+      for (int j = 0; j < valid; ++j) dst[j] = (uint8_t)(ow[j >> 2] >> (8 * (j & 3)));
+    }
+  }
+}
+
+constexpr size_t kColTSmem = 1024 + kCodeTileBytes + 128 * kTPitch + 128 * 128 + 4 * 128 * 4 +
+                             2 * 128 * 4 + 16;
+
+bool colT_attr() {
+  static const bool ok =
+      cudaFuncSetAttribute((const void*)fp8_colT_kernel<false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kColTSmem) ==
+          cudaSuccess &&
+      cudaFuncSetAttribute((const void*)fp8_colT_kernel<true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kColTSmem) ==
+          cudaSuccess;
+  return ok;
 }
 
 }  // namespace
@@ -294,9 +393,12 @@ extern "C" mxb_status mxb_per_token_Mxfp4ToFp8_col(const void* input, const void
               "mxfp4_to_fp8_col: null pointer");
   MXB_REQUIRE(aligned(input, 16) && aligned(input_s, 4) && aligned(output_q, 16),
               MXB_ERR_MISALIGNED, "mxfp4_to_fp8_col: misaligned pointer");
+  CUtensorMap tmap;
+  if (!make_tensor_map_2d(&tmap, input, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, Kb, Kb, 64, 128,
+                          CU_TENSOR_MAP_SWIZZLE_64B))
+    return MXB_ERR_CUDA;
   const dim3 grid((unsigned)(Kb / 64), (unsigned)(M / 128));
-  fp8_col_kernel<<<grid, kThreads, 0, to_cuda(stream)>>>((const uint8_t*)input,
-                                                         (const uint8_t*)input_s, M, Kb,
+  fp8_col_kernel<<<grid, kThreads, 0, to_cuda(stream)>>>(tmap, (const uint8_t*)input_s, M, Kb,
                                                          (uint8_t*)output_q, (float*)output_s);
   return launch_status("mxfp4_to_fp8_col");
 }
@@ -311,10 +413,15 @@ extern "C" mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col(const void* input, co
   MXB_REQUIRE(input && input_s && output_q && output_s, MXB_ERR_INVALID_ARGUMENT,
               "mxfp4_to_fp8_colT: null pointer");
   MXB_REQUIRE(aligned(input, 16), MXB_ERR_MISALIGNED, "mxfp4_to_fp8_colT: input not 16-byte aligned");
+  MXB_REQUIRE(colT_attr(), MXB_ERR_CUDA, "mxfp4_to_fp8_colT: cannot reserve shared memory");
+  CUtensorMap tmap;
+  if (!make_tensor_map_2d(&tmap, input, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, N / 2, N / 2, 64, 128,
+                          CU_TENSOR_MAP_SWIZZLE_64B))
+    return MXB_ERR_CUDA;
   const dim3 grid((unsigned)cdiv(M, 128), 1, (unsigned)cdiv(N, 128));
-  fp8_colT_kernel<false><<<grid, kThreads, 0, to_cuda(stream)>>>(
-      (const uint8_t*)input, (const uint8_t*)input_s, M, N, eps, (uint8_t*)output_q,
-      (float*)output_s, SplitArgs{nullptr, nullptr, nullptr});
+  fp8_colT_kernel<false><<<grid, kThreads, kColTSmem, to_cuda(stream)>>>(
+      tmap, (const uint8_t*)input_s, M, N, eps, (uint8_t*)output_q, (float*)output_s,
+      SplitArgs{nullptr, nullptr, nullptr});
   return launch_status("mxfp4_to_fp8_colT");
 }
 
@@ -334,9 +441,14 @@ extern "C" mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit(
               MXB_ERR_INVALID_ARGUMENT, "mxfp4_to_fp8_colT_msplit: null pointer");
   MXB_REQUIRE(aligned(input, 16), MXB_ERR_MISALIGNED,
               "mxfp4_to_fp8_colT_msplit: input not 16-byte aligned");
+  MXB_REQUIRE(colT_attr(), MXB_ERR_CUDA, "mxfp4_to_fp8_colT_msplit: cannot reserve shared memory");
+  CUtensorMap tmap;
+  if (!make_tensor_map_2d(&tmap, input, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, total_M, N / 2, N / 2,
+                          64, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+    return MXB_ERR_CUDA;
   const dim3 grid((unsigned)num_splits, (unsigned)cdiv(max_split_len, 128), (unsigned)cdiv(N, 128));
-  fp8_colT_kernel<true><<<grid, kThreads, 0, to_cuda(stream)>>>(
-      (const uint8_t*)input, (const uint8_t*)input_s, total_M, N, eps, (uint8_t*)output_q,
-      (float*)output_s, SplitArgs{m_splits, split_offsets, scale_offsets});
+  fp8_colT_kernel<true><<<grid, kThreads, kColTSmem, to_cuda(stream)>>>(
+      tmap, (const uint8_t*)input_s, total_M, N, eps, (uint8_t*)output_q, (float*)output_s,
+      SplitArgs{m_splits, split_offsets, scale_offsets});
   return launch_status("mxfp4_to_fp8_colT_msplit");
 }

@@ -8,7 +8,7 @@
 // else is one BF16x2 multiply per two outputs.
 //
 // DQ-fp8-row contract (code/kernel/per_token_Mxfp4ToFp8.cu:157-233), per 1x128
-// group of four E8M0 bytes:
+// group of four E8M0 bytes (evaluated through a table, fp8_lut.cuh):
 //   g   = (uint16)(max e - 6)       group scale float bits ((uint8)g) << 23
 //   adj = (uint16)(g - e)
 //   q   = E4M3(clamp(bf16(code_bits - (adj << 7) mod 2^16), +-448))
@@ -17,6 +17,7 @@
 // +-448 exactly as on the reference.
 #include "capi_util.h"
 #include "common.cuh"
+#include "fp8_lut.cuh"
 
 namespace mxb {
 namespace {
@@ -70,20 +71,14 @@ __global__ void __launch_bounds__(256) dq_bf16_kernel(const uint8_t* __restrict_
 // -------------------------------------------------------------- DQ-fp8-row
 // A lane converts 8 code bytes (16 elements, half a 32-element block) into one
 // 16-byte FP8 store; eight lanes cover one 1x128 group and read the group's
-// four E8M0 bytes as one word.
+// four E8M0 bytes as one word.  The element arithmetic is a lookup in the
+// compile-time table row for d = max_e - e (fp8_lut.cuh).
+__device__ const Fp8Lut g_lut_row = make_fp8_lut(false);
+
 __device__ __forceinline__ uint32_t max_u8x4(uint32_t s) {
   uint32_t a = max(s & 0xFFu, (s >> 8) & 0xFFu);
   uint32_t b = max((s >> 16) & 0xFFu, s >> 24);
   return max(a, b);
-}
-
-__device__ __forceinline__ uint32_t rebase_fp8x2(uint32_t x2, uint32_t off16) {
-  // x2: two BF16 code patterns; returns E4M3 of both re-based values
-  float lo = __uint_as_float((x2 << 16) - off16);
-  float hi = __uint_as_float((x2 & 0xFFFF0000u) - off16);
-  lo = fmaxf(-448.0f, fminf(448.0f, lo));
-  hi = fmaxf(-448.0f, fminf(448.0f, hi));
-  return cvt_e4m3x2(lo, hi);
 }
 
 __global__ void __launch_bounds__(256) dq_fp8_row_kernel(const uint8_t* __restrict__ codes,
@@ -97,14 +92,13 @@ __global__ void __launch_bounds__(256) dq_fp8_row_kernel(const uint8_t* __restri
   for (int64_t base = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) * 2;
        base < lanes_total; base += stride) {
     uint2 w[2];
-    uint32_t sw[2], e[2];
+    uint32_t sw[2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int64_t l = base + k * 32 + (threadIdx.x & 31);
       if (l < lanes_total) {
         w[k] = ld_stream_v2(codes + l * 8);
         sw[k] = ld_stream_u32(scales + (l >> 3) * 4);
-        e[k] = (sw[k] >> (8 * ((l >> 1) & 3))) & 0xFFu;
       }
     }
 #pragma unroll
@@ -112,24 +106,17 @@ __global__ void __launch_bounds__(256) dq_fp8_row_kernel(const uint8_t* __restri
       const int64_t l = base + k * 32 + (threadIdx.x & 31);
       if (l >= lanes_total) continue;
       const uint32_t mx = max_u8x4(sw[k]);
-      const uint32_t g = (mx - 6u) & 0xFFFFu;
-      const uint32_t adj = (g - e[k]) & 0xFFFFu;
-      const uint32_t off16 = ((adj << 7) & 0xFFFFu) << 16;
-      uint32_t o[4];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t cw = h ? w[k].y : w[k].x;
-        uint32_t x0, x1, x2, x3;
-        e2m1x4_to_bf16x4(cw, x0, x1);
-        e2m1x4_to_bf16x4(cw >> 16, x2, x3);
-        o[2 * h] = rebase_fp8x2(x0, off16) | (rebase_fp8x2(x1, off16) << 16);
-        o[2 * h + 1] = rebase_fp8x2(x2, off16) | (rebase_fp8x2(x3, off16) << 16);
-      }
-      st_stream_v4(out + l * 16, make_uint4(o[0], o[1], o[2], o[3]));
+      const uint32_t e = (sw[k] >> (8 * ((l >> 1) & 3))) & 0xFFu;
+      const uint4 t = __ldg(reinterpret_cast<const uint4*>(g_lut_row.v[mx - e]));
+      const uint4 o = make_uint4(lut_lookup4(w[k].x, t.x, t.y, t.z, t.w),
+                                 lut_lookup4(w[k].x >> 16, t.x, t.y, t.z, t.w),
+                                 lut_lookup4(w[k].y, t.x, t.y, t.z, t.w),
+                                 lut_lookup4(w[k].y >> 16, t.x, t.y, t.z, t.w));
+      st_stream_v4(out + l * 16, o);
       if ((l & 7) == 0) {
         const int64_t grp = l >> 3;
         const int64_t r = grp / groups_per_row, gc = grp - r * groups_per_row;
-        scales_out[gc * M + r] = __uint_as_float((g & 0xFFu) << 23);
+        scales_out[gc * M + r] = __uint_as_float(((mx - 6u) & 0xFFu) << 23);
       }
     }
   }

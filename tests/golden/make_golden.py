@@ -77,17 +77,21 @@ def fp8_cols(c, s):
 
 
 def fp8_colT(c, s):
+    """The reference kernel lacks a barrier (per_token_Mxfp4RowToBf16ToFp8Col.cu:126-131)
+    and its output varies from run to run; eight runs are kept and the bytes
+    on which all of them agree form the stability masks stored beside run 0."""
     M, Kb = c.shape
     N = 2 * Kb
     runs = []
-    for _ in range(3):
+    for _ in range(8):
         q = torch.empty(N, M, dtype=torch.float8_e4m3fn, device=dev)
         so = torch.empty((M + 127) // 128, N, dtype=torch.float32, device=dev)
         omo_ref.omo_per_token_Mxfp4RowToBf16ToFp8Col(torch.as_tensor(c).to(dev),
                                                     torch.as_tensor(s).to(dev), q, so, 1e-10)
         runs.append((u8(q), u8(so)))
-    stable = all(np.array_equal(runs[0][i], r[i]) for r in runs for i in range(2))
-    return runs[0][0], runs[0][1], stable
+    mq = np.logical_and.reduce([r[0] == runs[0][0] for r in runs])
+    ms = np.logical_and.reduce([r[1] == runs[0][1] for r in runs])
+    return runs[0][0], runs[0][1], mq, ms
 
 
 def fp8_colT_split(c, s, splits):
@@ -127,8 +131,8 @@ def main(out_path):
     c, s = syn.config3(256, 256, seed=21, lo=0, hi=255)
     g["fp8_cols_q"], g["fp8_cols_s"] = fp8_cols(c.numpy(), s.numpy())
     c, s = syn.config3(256, 128, seed=22, lo=117, hi=137)
-    g["fp8_colT_q"], g["fp8_colT_s"], stable = fp8_colT(c.numpy(), s.numpy())
-    g["fp8_colT_stable"] = np.array([stable])
+    g["fp8_colT_q"], g["fp8_colT_s"], g["fp8_colT_q_stable"], g["fp8_colT_s_stable"] = \
+        fp8_colT(c.numpy(), s.numpy())
     c, s = syn.config3(410, 80, seed=23, lo=100, hi=150)
     g["fp8_colT_split_q"], g["fp8_colT_split_s"] = fp8_colT_split(c.numpy(), s.numpy(),
                                                                   [5, 128, 200, 0, 77])
