@@ -36,8 +36,8 @@ M2, K2 = 16384, 8192
 ALG_BYTES_ROWCOL = M2 * K2 * 2 + 2 * (M2 * K2 // 2 + M2 * K2 // 32)  # 411,041,792
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the headline
-# kernel from one ncu capture (profiles/quant_rowcol_config2.md); None until measured.
-NCU_TRAFFIC_ROWCOL = None
+# kernel from one ncu capture (profiles/quant_rowcol_config2.md).
+NCU_TRAFFIC_ROWCOL = 268_590_592 + 109_284_864  # read + write inside the launch; the rest of the writes drain from L2 afterwards
 
 
 def measured_peaks():
