@@ -162,6 +162,29 @@ mxb_status mxb_per_token_quant_fp8(const void* input, int64_t M, int64_t K, void
 mxb_status mxb_per_token_dequant_fp8(const void* input_q, const void* input_s, int64_t M,
                                      int64_t K, void* output, mxb_stream_t stream);
 
+/* ------------------------------------------------------------ MoE expert parallel */
+
+/* Dispatch pack: quantizes each token row of x (bf16 [T, H], H % 128 == 0) to
+ * MXFP4 once (bit-exact Q-row, eps <= 6e-10) and writes its wire row
+ * codes[H/2] || scales[H/32] (megatron-0.15.0rc7.diff:32-63, the packing
+ * `fp4_quantize` hands to DeepEP at :290-297) to wire + slots[t*G + g] * (17H/32)
+ * for every g with slots[t*G + g] >= 0.  slots: int32 DEVICE array [T, G]. */
+mxb_status mxb_ep_pack(const void* x, int64_t T, int64_t H, const int32_t* slots, int G, void* wire,
+                       float eps, mxb_stream_t stream);
+
+/* Receive side: wire rows [R, 17H/32] -> bf16 [R, H], bit-exact with
+ * `get_fp4_tensor(recv_x).dequantize()` (megatron-0.15.0rc7.diff:101-124,303-309).
+ * If weight (float DEVICE [R]) is given, each row is multiplied by weight[row]
+ * after the dequantize and rounded to bf16 again. */
+mxb_status mxb_ep_unpack(const void* wire, int64_t R, int64_t H, const float* weight, void* out,
+                         mxb_stream_t stream);
+
+/* Combine: out[t] = bf16(sum over g = 0..G-1 with slots[t*G + g] >= 0 of
+ * float(recv[slots[t*G + g]])), summed in rank order; recv bf16 [S, H],
+ * out bf16 [T, H].  The BF16 combine of DeepEP (deep_ep-1.2.1.diff:132-139). */
+mxb_status mxb_ep_combine(const void* recv, int64_t T, int64_t H, const int32_t* slots, int G,
+                          void* out, mxb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,229 @@
+// MoE expert-parallel dispatch / combine kernels with MXFP4 payloads (sm_100a).
+//
+// Wire row of one token (megatron-0.15.0rc7.diff:32-63, `_pack_rowwise_components`):
+//     codes[H/2] || E8M0 scales[H/32]        (row_bytes = 17 H / 32; 3808 B at H = 7168)
+// The reference quantizes the tokens (Q-row), concatenates codes and scales along
+// the last dimension and hands the rows to DeepEP's dispatch; the receiver splits
+// them at 16/17 and dequantizes (C2) (megatron-0.15.0rc7.diff:91-124,290-311).
+//
+//  * ep_pack: one CTA per token quantizes the row once (bit-exact Q-row) and
+//    writes its wire row to every destination slot slots[t, g] >= 0, so a token
+//    routed to several ranks is read from HBM once.
+//  * ep_unpack: wire rows -> BF16 (bit-exact C2); optionally times a per-row
+//    FP32 weight (the routing-weighted identity expert of the benchmark).
+//  * ep_combine: out[t] = bf16(sum over g = 0..G-1 of float(recv[slots[t, g]])),
+//    summed in rank order (deterministic).
+#include <cuda_bf16.h>
+
+#include "capi_util.h"
+#include "common.cuh"
+
+namespace mxb {
+namespace {
+
+constexpr int kEpThreads = 256;
+
+// Q-row of one 32-element block held as 16 BF16 pairs (fast path: fp4_max = 6,
+// eps <= 6e-10), same arithmetic as the quantize kernels.
+__device__ __forceinline__ void ep_quant_block(const uint32_t (&w)[16], uint32_t (&out)[4],
+                                               uint32_t& byte, float eps) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m = vmax_u16x2(m, w[i] & 0x7FFF7FFFu);
+  const uint32_t mb = max(m & 0xFFFFu, m >> 16);
+  if (mb < 0x7F80u) {
+    int k = (int)(mb >> 7) - 129 + ((mb & 0x7Fu) > 0x40u ? 1 : 0);
+    k = k < -33 ? -33 : k;
+    byte = (uint32_t)(k + 127);
+    const float inv = __uint_as_float((uint32_t)(127 - k) << 23);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[2 * j] = bf16lo_to_f(w[4 * i + j]) * inv;
+        v[2 * j + 1] = bf16hi_to_f(w[4 * i + j]) * inv;
+      }
+      out[i] = cvt_e2m1x8(v);
+    }
+  } else {
+    // Inf / NaN in the block: the reference formula literally
+    float a = eps;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a = fmaxf(a, fmaxf(fabsf(bf16lo_to_f(w[i])), fabsf(bf16hi_to_f(w[i]))));
+    float y = exp2f(ceilf(log2f(fmaxf(a / 6.0f, 1e-10f))));
+    byte = ((uint32_t)(int)log2f(y) + 127u) & 0xFFu;
+    const float inv = 1.0f / y;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t r = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t wj = w[4 * i + j / 2];
+        float q = (j & 1) ? bf16hi_to_f(wj) : bf16lo_to_f(wj);
+        q = fminf(fmaxf(q * inv, -6.0f), 6.0f);
+        // E2M1 RNE with the sign kept, the reference's integer rounding
+        const uint32_t b = __float_as_uint(q);
+        const uint32_t sign = b >> 28 & 0x8u;
+        uint32_t ex = (b >> 23) & 0xFFu, man = b & 0x7FFFFFu;
+        if (ex < 127u) {
+          const uint32_t sh = 126u - ex;
+          man = sh >= 32u ? 0u : ((0x400000u | (man >> 1)) >> sh);
+        }
+        ex = (ex > 126u ? ex : 126u) - 126u;
+        const uint32_t m2 = man >> 21;
+        const uint32_t inc = (m2 & 1u) & (((man & 0x1FFFFFu) != 0u) | ((m2 >> 1) & 1u));
+        uint32_t c = (((ex << 2) | m2) + inc) >> 1;
+        c = c > 7u ? 7u : c;
+        r |= (sign | c) << (4 * j);
+      }
+      out[i] = r;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kEpThreads) ep_pack_kernel(const uint8_t* __restrict__ x,
+                                                             int64_t T, int64_t H,
+                                                             const int32_t* __restrict__ slots,
+                                                             int G, uint8_t* __restrict__ wire,
+                                                             int64_t row_bytes, float eps) {
+  __shared__ int32_t dst[64];
+  const int64_t nb = H / 32;
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    if (threadIdx.x < G) dst[threadIdx.x] = slots[t * G + threadIdx.x];
+    __syncthreads();
+    const uint8_t* xr = x + t * H * 2;
+    for (int64_t b = threadIdx.x; b < nb; b += kEpThreads) {
+      const uint4 a0 = ld_stream_v4(xr + b * 64), a1 = ld_stream_v4(xr + b * 64 + 16);
+      const uint4 a2 = ld_stream_v4(xr + b * 64 + 32), a3 = ld_stream_v4(xr + b * 64 + 48);
+      const uint32_t w[16] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w,
+                              a2.x, a2.y, a2.z, a2.w, a3.x, a3.y, a3.z, a3.w};
+      uint32_t out[4], byte;
+      ep_quant_block(w, out, byte, eps);
+      for (int g = 0; g < G; ++g) {
+        const int32_t s = dst[g];
+        if (s < 0) continue;
+        uint8_t* row = wire + (int64_t)s * row_bytes;
+        uint32_t* c = reinterpret_cast<uint32_t*>(row + b * 16);
+        c[0] = out[0]; c[1] = out[1]; c[2] = out[2]; c[3] = out[3];
+        row[H / 2 + b] = (uint8_t)byte;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// wire rows -> BF16 (optionally x weight[row]); a thread handles 4 code bytes.
+__global__ void __launch_bounds__(kEpThreads) ep_unpack_kernel(const uint8_t* __restrict__ wire,
+                                                               int64_t R, int64_t H,
+                                                               int64_t row_bytes,
+                                                               const float* __restrict__ weight,
+                                                               uint8_t* __restrict__ out) {
+  const int64_t chunks = H / 8;  // 4 code bytes = 8 elements per chunk
+  for (int64_t r = blockIdx.x; r < R; r += gridDim.x) {
+    const uint8_t* row = wire + r * row_bytes;
+    const float wt = weight ? weight[r] : 1.0f;
+    for (int64_t c = threadIdx.x; c < chunks; c += kEpThreads) {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(row + c * 4);
+      const uint32_t e = row[H / 2 + (c >> 2)];
+      uint32_t o[4];
+      e2m1x4_to_bf16x4(w, o[0], o[1]);
+      e2m1x4_to_bf16x4(w >> 16, o[2], o[3]);
+      if (e - 2u <= 252u) {
+        const uint32_t s2 = (e << 7) | (e << 23);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = mul_bf16x2(o[i], s2);
+      } else {
+        const float s = e8m0_to_f(e);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = cvt_bf16x2(bf16lo_to_f(o[i]) * s, bf16hi_to_f(o[i]) * s);
+      }
+      if (weight) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = cvt_bf16x2(bf16lo_to_f(o[i]) * wt, bf16hi_to_f(o[i]) * wt);
+      }
+      *reinterpret_cast<uint4*>(out + (r * H + c * 8) * 2) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// out[t] = bf16(sum_g float(recv[slots[t, g]])) in rank order.
+__global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(const uint8_t* __restrict__ recv,
+                                                                int64_t T, int64_t H,
+                                                                const int32_t* __restrict__ slots,
+                                                                int G, uint8_t* __restrict__ out) {
+  __shared__ int32_t src[64];
+  const int64_t chunks = H / 8;
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    if (threadIdx.x < G) src[threadIdx.x] = slots[t * G + threadIdx.x];
+    __syncthreads();
+    for (int64_t c = threadIdx.x; c < chunks; c += kEpThreads) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int g = 0; g < G; ++g) {
+        const int32_t s = src[g];
+        if (s < 0) continue;
+        const uint4 v = *reinterpret_cast<const uint4*>(recv + ((int64_t)s * H + c * 8) * 2);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[2 * i] += bf16lo_to_f(w[i]);
+          acc[2 * i + 1] += bf16hi_to_f(w[i]);
+        }
+      }
+      *reinterpret_cast<uint4*>(out + (t * H + c * 8) * 2) =
+          make_uint4(cvt_bf16x2(acc[0], acc[1]), cvt_bf16x2(acc[2], acc[3]),
+                     cvt_bf16x2(acc[4], acc[5]), cvt_bf16x2(acc[6], acc[7]));
+    }
+    __syncthreads();
+  }
+}
+
+int ep_grid(int64_t rows) { return (int)(rows < 148LL * 16 ? (rows > 0 ? rows : 1) : 148LL * 16); }
+
+}  // namespace
+}  // namespace mxb
+
+using namespace mxb;
+
+extern "C" mxb_status mxb_ep_pack(const void* x, int64_t T, int64_t H, const int32_t* slots,
+                                  int G, void* wire, float eps, mxb_stream_t stream) {
+  MXB_REQUIRE(T >= 0 && H > 0 && H % 128 == 0 && G >= 1 && G <= 64, MXB_ERR_INVALID_ARGUMENT,
+              "ep_pack: need H %% 128 == 0 and 1 <= G <= 64 (H=%lld G=%d)", (long long)H, G);
+  MXB_REQUIRE(eps >= 0.0f && eps <= 6e-10f, MXB_ERR_UNSUPPORTED,
+              "ep_pack: eps must be in [0, 6e-10] (the dispatch quantizer's configuration)");
+  if (T == 0) return MXB_OK;
+  MXB_REQUIRE(x && slots && wire, MXB_ERR_INVALID_ARGUMENT, "ep_pack: null pointer");
+  const int64_t row_bytes = H / 2 + H / 32;
+  MXB_REQUIRE(aligned(x, 16) && aligned(wire, 4) && row_bytes % 4 == 0, MXB_ERR_MISALIGNED,
+              "ep_pack: x must be 16-byte and wire rows 4-byte aligned");
+  ep_pack_kernel<<<ep_grid(T), kEpThreads, 0, to_cuda(stream)>>>(
+      (const uint8_t*)x, T, H, slots, G, (uint8_t*)wire, row_bytes, eps);
+  return launch_status("ep_pack");
+}
+
+extern "C" mxb_status mxb_ep_unpack(const void* wire, int64_t R, int64_t H, const float* weight,
+                                    void* out, mxb_stream_t stream) {
+  MXB_REQUIRE(R >= 0 && H > 0 && H % 128 == 0, MXB_ERR_INVALID_ARGUMENT,
+              "ep_unpack: need H %% 128 == 0 (H=%lld)", (long long)H);
+  if (R == 0) return MXB_OK;
+  MXB_REQUIRE(wire && out, MXB_ERR_INVALID_ARGUMENT, "ep_unpack: null pointer");
+  const int64_t row_bytes = H / 2 + H / 32;
+  MXB_REQUIRE(aligned(wire, 4) && row_bytes % 4 == 0 && aligned(out, 16), MXB_ERR_MISALIGNED,
+              "ep_unpack: wire rows must be 4-byte and out 16-byte aligned");
+  ep_unpack_kernel<<<ep_grid(R), kEpThreads, 0, to_cuda(stream)>>>(
+      (const uint8_t*)wire, R, H, row_bytes, weight, (uint8_t*)out);
+  return launch_status("ep_unpack");
+}
+
+extern "C" mxb_status mxb_ep_combine(const void* recv, int64_t T, int64_t H, const int32_t* slots,
+                                     int G, void* out, mxb_stream_t stream) {
+  MXB_REQUIRE(T >= 0 && H > 0 && H % 8 == 0 && G >= 1 && G <= 64, MXB_ERR_INVALID_ARGUMENT,
+              "ep_combine: need H %% 8 == 0 and 1 <= G <= 64");
+  if (T == 0) return MXB_OK;
+  MXB_REQUIRE(recv && slots && out, MXB_ERR_INVALID_ARGUMENT, "ep_combine: null pointer");
+  MXB_REQUIRE(aligned(recv, 16) && aligned(out, 16), MXB_ERR_MISALIGNED,
+              "ep_combine: recv and out must be 16-byte aligned");
+  ep_combine_kernel<<<ep_grid(T), kEpThreads, 0, to_cuda(stream)>>>(
+      (const uint8_t*)recv, T, H, slots, G, (uint8_t*)out);
+  return launch_status("ep_combine");
+}

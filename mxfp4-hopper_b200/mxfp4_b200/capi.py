@@ -32,6 +32,9 @@ SIGNATURES = {
                                                     _I64, _I64, _F, _P],
     "mxb_per_token_quant_fp8": [_P, _I64, _I64, _P, _P, _F, _P],
     "mxb_per_token_dequant_fp8": [_P, _P, _I64, _I64, _P, _P],
+    "mxb_ep_pack": [_P, _I64, _I64, _P, _I, _P, _F, _P],
+    "mxb_ep_unpack": [_P, _I64, _I64, _P, _P, _P],
+    "mxb_ep_combine": [_P, _I64, _I64, _P, _I, _P, _P],
 }
 
 STATUS = {0: "MXB_OK", 1: "MXB_ERR_INVALID_ARGUMENT", 2: "MXB_ERR_MISALIGNED", 3: "MXB_ERR_CUDA",

@@ -1,0 +1,96 @@
+"""Expert-parallel data kernels on the GPU (through the C ABI) against the
+oracle, and the full NCCL dispatch -> identity experts -> combine round on
+2+ GPUs (one process per GPU)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from ep_oracle import combine_rows, expected_round, pack_rows, unpack_rows
+from mxfp4_b200 import synthetic as syn
+from mxfp4_b200.ep import CudaKernels, build_route, weight_sums
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("world,T,H", [(1, 7, 128), (4, 200, 512), (8, 512, 7168)])
+def test_pack_unpack_combine_kernels(cuda, world, T, H):
+    x, idx, w = syn.config5(0, world, tokens=T, hidden=H)
+    if T > 100:  # a few blocks with Inf / NaN / zeros
+        xb = syn.bf16_bits(x).copy()
+        xb[3, 5], xb[4, 70], xb[5, :] = 0x7F80, 0xFFC1, 0
+        x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16)
+    r = build_route(idx, w, world, 256)
+    S = int(r.send_counts.sum())
+    K = CudaKernels()
+    wire = K.pack(x.to(cuda), r.slots.to(cuda), S)
+    rows = pack_rows(x)
+    assert np.array_equal(wire.cpu().numpy(), rows[r.src_token.numpy()])
+    wsum = weight_sums(r.local_w)
+    y = K.unpack(wire, H, wsum.to(cuda))
+    y_ref = unpack_rows(wire.cpu().numpy(), H, wsum.numpy())
+    assert np.array_equal(y.cpu().view(torch.int16).numpy().view(np.uint16), y_ref)
+    y0 = K.unpack(wire, H, None)
+    assert np.array_equal(y0.cpu().view(torch.int16).numpy().view(np.uint16),
+                          unpack_rows(wire.cpu().numpy(), H))
+    out = K.combine(y, r.slots.to(cuda))
+    assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16),
+                          combine_rows(y_ref, r.slots.numpy()))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    try:
+        import sys
+        from pathlib import Path
+        root = Path(__file__).resolve().parent.parent
+        for p in (root, root / "mxfp4-hopper_b200", root / "tests"):
+            sys.path.insert(0, str(p))
+        import torch.distributed as dist
+        from ep_oracle import expected_round
+        from mxfp4_b200 import synthetic as syn
+        from mxfp4_b200.ep import MXFP4Dispatcher
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, device_id=dev)
+        x, idx, w = syn.config5(rank, world, tokens=512, hidden=7168)
+        d = MXFP4Dispatcher(None, num_experts=256, hidden=7168)
+        recv_wire, recv_topk, recv_w, h = d.dispatch(x.to(dev), idx.to(dev), w.to(dev))
+        out = d.combine(d.identity_experts(recv_wire, recv_w), h)
+        exp = expected_round(x, idx, w, world, 256)
+        ok = np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), exp)
+        q.put((rank, ok))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+def test_dispatch_combine_nccl():
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs 2 GPUs")
+    world = min(n, 8)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok in sorted(res):
+        assert ok is True, f"rank {rank}: {ok}"
