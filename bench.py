@@ -263,6 +263,7 @@ def main():
     del xh, outs_h
 
     ops = {} if args.no_ops else time_other_ops(dev, stream, peak)
+    ep = time_ep(dev, stream, world, rank, args) if world > 1 else None
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -288,11 +289,66 @@ def main():
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
         "ops": ops,
+        "ep": ep,
     }
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool (900 nominal)
+
+
+def time_ep(dev, stream, world, rank, args):
+    """MoE dispatch -> identity experts -> combine (config 5): 4096 tokens per
+    rank, H = 7168, top-8 of 256 experts, MXFP4 payload out, BF16 back.
+    Returns tokens/s over the whole job and the NVLink roofline fraction."""
+    import torch
+    import torch.distributed as dist
+
+    from mxfp4_b200 import synthetic as syn
+    from mxfp4_b200.ep import MXFP4Dispatcher, build_route, wire_row_bytes
+
+    T, H = 4096, 7168
+    x, idx, w = (t.to(dev) for t in syn.config5(rank, world, tokens=T, hidden=H))
+    d = MXFP4Dispatcher(None, num_experts=256, hidden=H)
+
+    def step():
+        rw, rt, rwt, h = d.dispatch(x, idx, w)
+        return d.combine(d.identity_experts(rw, rwt), h), h
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    n = max(5, min(args.steps, 20))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        _, h = step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / n
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # bytes that must cross NVLink per GPU and direction (payload + 64 B of routing metadata per row)
+    rb = wire_row_bytes(H) + 64
+    send_remote = sum(c for g, c in enumerate(h.send_splits) if g != rank)
+    recv_remote = sum(c for g, c in enumerate(h.recv_splits) if g != rank)
+    out_bytes = send_remote * rb + recv_remote * H * 2      # dispatch out + combine out
+    in_bytes = recv_remote * rb + send_remote * H * 2
+    bt = torch.tensor([float(max(out_bytes, in_bytes))], dtype=torch.float64, device=dev)
+    dist.all_reduce(bt, op=dist.ReduceOp.MAX)
+    floor_ms = float(bt.item()) / (NVLINK_GBS * 1e9) * 1e3
+    return {"metric": "ep_dispatch_combine_tokens_per_s", "value": round(world * T / (ms * 1e-3), 1),
+            "unit": "tokens/s", "ms_per_step": round(ms, 4), "tokens_per_rank": T, "hidden": H,
+            "experts": 256, "topk": 8, "payload": "mxfp4 dispatch, bf16 combine",
+            "transport": "NCCL all_to_all_single (torch.distributed)",
+            "nvlink_roofline": {"bound": "nvlink", "bytes_per_gpu_direction": int(bt.item()),
+                                "peak_gbs": NVLINK_GBS, "floor_ms": round(floor_ms, 4),
+                                "frac": round(floor_ms / ms, 4)}}
 
 
 def time_other_ops(dev, stream, peak):
