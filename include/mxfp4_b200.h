@@ -185,6 +185,63 @@ mxb_status mxb_ep_unpack(const void* wire, int64_t R, int64_t H, const float* we
 mxb_status mxb_ep_combine(const void* recv, int64_t T, int64_t H, const int32_t* slots, int G,
                           void* out, mxb_stream_t stream);
 
+/* ---- fused dispatch / combine over NVLink peer memory ----
+ * One buffer per rank with the layout below, mapped into every peer with CUDA
+ * IPC (mxb_ipc_export / mxb_ipc_import); `bases` is a DEVICE array of the world
+ * base addresses (this rank's own buffer at index rank).  A step is
+ *   mxb_ep_p2p_counts(epoch e+1)  -> every rank learns every send count
+ *   mxb_ep_p2p_dispatch            -> tokens quantized once and stored into the
+ *                                     destinations' receive rows over NVLink
+ *   mxb_ep_p2p_barrier(e+2)
+ *   mxb_ep_p2p_return              -> expert rows stored back into the sources
+ *   mxb_ep_p2p_barrier(e+3)
+ *   mxb_ep_combine on this rank's back rows.
+ * The same semantics as DeepEP's intranode dispatch/combine with the MXFP4
+ * payload of the reference (deep_ep-1.2.1.diff:455-549, megatron-0.15.0rc7.diff:
+ * 290-311), without host synchronisation.  Parity alternates per step.  All
+ * cross-GPU waits are bounded; mxb_ep_wait_timeouts() counts waits that gave up. */
+typedef struct {
+  int64_t sig_off, cnt_off, wire_off, meta_off, back_off; /* byte offsets in the buffer */
+  int64_t tcap;                                           /* max tokens per rank */
+  int32_t world, rank, topk, hidden, experts_per_rank;
+} mxb_ep_layout;
+
+mxb_status mxb_ep_layout_init(int32_t world, int32_t rank, int64_t tcap, int32_t hidden,
+                              int32_t topk, int32_t experts_per_rank, mxb_ep_layout* layout,
+                              int64_t* total_bytes);
+/* CUDA IPC of a device allocation: 64-byte handle + offset of ptr in it. */
+mxb_status mxb_ipc_export(const void* ptr, void* handle64, int64_t* offset);
+mxb_status mxb_ipc_import(const void* handle64, int64_t offset, void** ptr);
+mxb_status mxb_ipc_close(void* ptr, int64_t offset);
+/* send_counts: int32 DEVICE [world]. */
+mxb_status mxb_ep_p2p_counts(const uint64_t* bases, const mxb_ep_layout* layout,
+                             const int32_t* send_counts, int parity, uint32_t epoch,
+                             mxb_stream_t stream);
+/* x bf16 [T, hidden]; within int32 DEVICE [T, world]: index of token t among the
+ * tokens this rank sends to rank g, or -1; topk_idx int64 / topk_w float DEVICE
+ * [T, topk] global expert ids and routing weights. */
+mxb_status mxb_ep_p2p_dispatch(const void* x, int64_t T, const int32_t* within,
+                               const int64_t* topk_idx, const float* topk_w,
+                               const uint64_t* bases, const mxb_ep_layout* layout, int parity,
+                               mxb_stream_t stream);
+mxb_status mxb_ep_p2p_barrier(const uint64_t* bases, const mxb_ep_layout* layout, uint32_t epoch,
+                              mxb_stream_t stream);
+/* y: bf16 DEVICE [world*tcap, hidden] expert outputs per received row, or NULL
+ * for the routing-weighted identity expert fused with the dequantize. */
+mxb_status mxb_ep_p2p_return(const void* y, const uint64_t* bases, const mxb_ep_layout* layout,
+                             int parity, mxb_stream_t stream);
+/* Routing on the device: within[t*world + g] = index of token t among the
+ * tokens routed to rank g (experts contiguous per rank, topk_idx int64
+ * [T, topk] global ids), -1 if none; send_counts[g] = number of such tokens. */
+mxb_status mxb_ep_route(const int64_t* topk_idx, int64_t T, int32_t topk, int32_t experts_per_rank,
+                        int32_t world, int32_t* within, int32_t* send_counts, mxb_stream_t stream);
+/* Local combine of the returned rows: out[t] = bf16(sum over g of
+ * float(back[sum_{g'<g} send_counts[g'] + within[t, g]])). */
+mxb_status mxb_ep_p2p_combine(const void* back, int64_t T, int64_t H, const int32_t* within,
+                              const int32_t* send_counts, int32_t world, void* out,
+                              mxb_stream_t stream);
+unsigned int mxb_ep_wait_timeouts(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,6 +37,32 @@ SIGNATURES = {
     "mxb_ep_combine": [_P, _I64, _I64, _P, _I, _P, _P],
 }
 
+class EpLayout(ctypes.Structure):
+    """mxb_ep_layout of include/mxfp4_b200.h."""
+    _fields_ = [("sig_off", ctypes.c_int64), ("cnt_off", ctypes.c_int64),
+                ("wire_off", ctypes.c_int64), ("meta_off", ctypes.c_int64),
+                ("back_off", ctypes.c_int64), ("tcap", ctypes.c_int64),
+                ("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("topk", ctypes.c_int32),
+                ("hidden", ctypes.c_int32), ("experts_per_rank", ctypes.c_int32)]
+
+
+_LP = ctypes.POINTER(EpLayout)
+_U32 = ctypes.c_uint32
+
+SIGNATURES.update({
+    "mxb_ep_layout_init": [ctypes.c_int32, ctypes.c_int32, _I64, ctypes.c_int32, ctypes.c_int32,
+                           ctypes.c_int32, _LP, ctypes.POINTER(ctypes.c_int64)],
+    "mxb_ipc_export": [_P, _P, ctypes.POINTER(ctypes.c_int64)],
+    "mxb_ipc_import": [_P, _I64, ctypes.POINTER(ctypes.c_void_p)],
+    "mxb_ipc_close": [_P, _I64],
+    "mxb_ep_p2p_counts": [_P, _LP, _P, _I, _U32, _P],
+    "mxb_ep_p2p_dispatch": [_P, _I64, _P, _P, _P, _P, _LP, _I, _P],
+    "mxb_ep_p2p_barrier": [_P, _LP, _U32, _P],
+    "mxb_ep_p2p_return": [_P, _P, _LP, _I, _P],
+    "mxb_ep_route": [_P, _I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, _P, _P],
+    "mxb_ep_p2p_combine": [_P, _I64, _I64, _P, _P, ctypes.c_int32, _P, _P],
+})
+
 STATUS = {0: "MXB_OK", 1: "MXB_ERR_INVALID_ARGUMENT", 2: "MXB_ERR_MISALIGNED", 3: "MXB_ERR_CUDA",
           4: "MXB_ERR_UNSUPPORTED"}
 
@@ -65,6 +91,7 @@ def load() -> ctypes.CDLL:
         L.mxb_last_error.restype = ctypes.c_char_p
         L.mxb_version.restype = ctypes.c_char_p
         L.mxb_wait_timeouts.restype = ctypes.c_uint
+        L.mxb_ep_wait_timeouts.restype = ctypes.c_uint
         _lib = L
     return _lib
 

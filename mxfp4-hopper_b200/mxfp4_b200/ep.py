@@ -168,3 +168,112 @@ class MXFP4Dispatcher:
         back = torch.empty(sum(handle.send_splits), y.shape[1], dtype=y.dtype, device=y.device)
         self._a2a(back, y, handle.send_splits, handle.recv_splits)
         return self.k.combine(back, handle.route.slots)
+
+
+def local_route(topk_idx: torch.Tensor, world: int, num_experts: int):
+    """Device-side routing without host synchronisation: (within int32 [T, G],
+    send_counts int32 [G], slots int32 [T, G]) where within[t, g] is token t's
+    index among the tokens sent to rank g (-1 if none) and slots[t, g] its row
+    in this rank's send order (grouped by destination)."""
+    T = topk_idx.shape[0]
+    per_rank = num_experts // world
+    dest = torch.div(topk_idx, per_rank, rounding_mode="floor")
+    mask = torch.zeros(T, world, dtype=torch.bool, device=topk_idx.device)
+    mask.scatter_(1, dest, True)
+    m64 = mask.to(torch.int64)
+    send_counts = m64.sum(0)
+    within = torch.where(mask, torch.cumsum(m64, 0) - 1, torch.full_like(m64, -1))
+    offsets = torch.cumsum(send_counts, 0) - send_counts
+    slots = torch.where(mask, offsets[None, :] + within, torch.full_like(m64, -1))
+    return within.to(torch.int32), send_counts.to(torch.int32), slots.to(torch.int32)
+
+
+class P2PDispatcher:
+    """Fused dispatch / combine over NVLink peer memory (one process per GPU).
+
+    Each rank owns one buffer (mxb_ep_layout) mapped into every peer with CUDA
+    IPC.  A step runs five kernels and no host synchronisation: count exchange,
+    fused quantize + peer store of the wire rows, barrier, expert stage fused
+    with the peer store of its output rows, barrier; then the local combine.
+    """
+
+    def __init__(self, group=None, tcap: int = 4096, hidden: int = 7168, topk: int = 8,
+                 num_experts: int = 256):
+        import ctypes
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.hidden, self.topk, self.num_experts, self.tcap = hidden, topk, num_experts, tcap
+        self.layout = capi.EpLayout()
+        total = ctypes.c_int64()
+        capi.call("mxb_ep_layout_init", self.world, self.rank, tcap, hidden, topk,
+                  num_experts // self.world, ctypes.byref(self.layout), ctypes.byref(total))
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.buf = torch.zeros(total.value, dtype=torch.uint8, device=dev)
+        torch.cuda.synchronize(dev)
+        handle = (ctypes.c_char * 64)()
+        off = ctypes.c_int64()
+        capi.call("mxb_ipc_export", self.buf.data_ptr(), ctypes.cast(handle, ctypes.c_void_p),
+                  ctypes.byref(off))
+        objs = [None] * self.world
+        dist.all_gather_object(objs, (bytes(handle), off.value), group=group)
+        self._imported = []
+        ptrs = []
+        for p, (h, o) in enumerate(objs):
+            if p == self.rank:
+                ptrs.append(self.buf.data_ptr())
+                continue
+            hb = (ctypes.c_char * 64).from_buffer_copy(h)
+            ptr = ctypes.c_void_p()
+            capi.call("mxb_ipc_import", ctypes.cast(hb, ctypes.c_void_p), o, ctypes.byref(ptr))
+            self._imported.append((ptr.value, o))
+            ptrs.append(ptr.value)
+        self.bases = torch.tensor([p if p < 2**63 else p - 2**64 for p in ptrs], dtype=torch.int64,
+                                  device=dev)
+        self.step_no = 0
+        dist.barrier(group=group)
+        L = self.layout
+        self.back = self.buf[L.back_off:L.back_off + self.world * tcap * hidden * 2].view(
+            torch.bfloat16).view(self.world * tcap, hidden)
+        self.wire = self.buf[L.wire_off:L.wire_off + self.world * tcap * wire_row_bytes(hidden)].view(
+            self.world * tcap, wire_row_bytes(hidden))
+
+    def close(self):
+        for ptr, o in self._imported:
+            capi.status_of("mxb_ipc_close", ptr, o)
+        self._imported = []
+
+    def _args(self):
+        import ctypes
+        return self.bases.data_ptr(), ctypes.byref(self.layout)
+
+    def step(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor,
+             expert_fn=None) -> torch.Tensor:
+        """Dispatch -> experts -> combine.  Without expert_fn every expert is the
+        identity and a row returns as its dequantized token times its local
+        routing-weight sum (fused into the return kernel)."""
+        T = x.shape[0]
+        s = torch.cuda.current_stream(x.device).cuda_stream
+        topk_idx = topk_idx.to(torch.int64).contiguous()
+        within = torch.empty(T, self.world, dtype=torch.int32, device=x.device)
+        send_counts = torch.empty(self.world, dtype=torch.int32, device=x.device)
+        capi.call("mxb_ep_route", topk_idx.data_ptr(), T, topk_idx.shape[1],
+                  self.num_experts // self.world, self.world, within.data_ptr(),
+                  send_counts.data_ptr(), s)
+        parity = self.step_no & 1
+        e = 3 * self.step_no
+        bases, lp = self._args()
+        capi.call("mxb_ep_p2p_counts", bases, lp, send_counts.data_ptr(), parity, e + 1, s)
+        capi.call("mxb_ep_p2p_dispatch", x.data_ptr(), T, within.data_ptr(),
+                  topk_idx.data_ptr(),
+                  topk_w.float().contiguous().data_ptr(), bases, lp, parity, s)
+        capi.call("mxb_ep_p2p_barrier", bases, lp, e + 2, s)
+        y = None if expert_fn is None else expert_fn(self.wire).contiguous()
+        capi.call("mxb_ep_p2p_return", None if y is None else y.data_ptr(), bases, lp, parity, s)
+        capi.call("mxb_ep_p2p_barrier", bases, lp, e + 3, s)
+        out = torch.empty(T, self.hidden, dtype=torch.bfloat16, device=x.device)
+        capi.call("mxb_ep_p2p_combine", self.back.data_ptr(), T, self.hidden, within.data_ptr(),
+                  send_counts.data_ptr(), self.world, out.data_ptr(), s)
+        self.step_no += 1
+        return out

@@ -41,6 +41,20 @@ def test_pack_unpack_combine_kernels(cuda, world, T, H):
                           combine_rows(y_ref, r.slots.numpy()))
 
 
+@pytest.mark.parametrize("world,T", [(1, 5), (2, 4096), (8, 4096), (8, 3000)])
+def test_route_kernel(cuda, world, T):
+    from mxfp4_b200 import capi
+    from mxfp4_b200.ep import local_route
+    _, idx, _ = syn.config5(3, world, tokens=T, hidden=128)
+    idx = idx.to(cuda).contiguous()
+    within = torch.empty(T, world, dtype=torch.int32, device=cuda)
+    counts = torch.empty(world, dtype=torch.int32, device=cuda)
+    capi.call("mxb_ep_route", idx.data_ptr(), T, 8, 256 // world, world, within.data_ptr(),
+              counts.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    w_ref, c_ref, _ = local_route(idx, world, 256)
+    assert torch.equal(within, w_ref) and torch.equal(counts, c_ref)
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -66,13 +80,26 @@ def _worker(rank, world, port, q):
         os.environ["NCCL_NVLS_ENABLE"] = "0"
         dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                                 world_size=world, device_id=dev)
+        from mxfp4_b200 import capi
+        from mxfp4_b200.ep import P2PDispatcher
         x, idx, w = syn.config5(rank, world, tokens=512, hidden=7168)
+        exp = expected_round(x, idx, w, world, 256)
         d = MXFP4Dispatcher(None, num_experts=256, hidden=7168)
         recv_wire, recv_topk, recv_w, h = d.dispatch(x.to(dev), idx.to(dev), w.to(dev))
         out = d.combine(d.identity_experts(recv_wire, recv_w), h)
-        exp = expected_round(x, idx, w, world, 256)
-        ok = np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), exp)
-        q.put((rank, ok))
+        ok_nccl = np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), exp)
+        p2p = P2PDispatcher(None, tcap=512, hidden=7168, topk=8, num_experts=256)
+        ok_p2p = True
+        for it in range(3):  # several steps: parity and epochs advance
+            xs, ids, ws = syn.config5(rank + 100 * it, world, tokens=512 - 64 * it, hidden=7168)
+            o2 = p2p.step(xs.to(dev), ids.to(dev), ws.to(dev))
+            e2 = expected_round(xs, ids, ws, world, 256)
+            ok_p2p &= np.array_equal(o2.cpu().view(torch.int16).numpy().view(np.uint16), e2)
+        torch.cuda.synchronize()
+        ok_p2p &= capi.load().mxb_ep_wait_timeouts() == 0
+        dist.barrier()
+        p2p.close()
+        q.put((rank, bool(ok_nccl and ok_p2p) or f"nccl {ok_nccl} p2p {ok_p2p}"))
         dist.destroy_process_group()
     except Exception as e:
         q.put((rank, repr(e)))
