@@ -44,14 +44,15 @@ __device__ __forceinline__ uint4 ld_code_chunk(const uint8_t* tile, int r, int c
 // Loads the tile with one TMA and waits (bounded).  Returns false, for every
 // thread of the CTA, if the copy never completed.
 __device__ __forceinline__ bool load_code_tile(uint8_t* tile, uint64_t* bar, const CUtensorMap* map,
-                                               int32_t x, int32_t y) {
+                                               int32_t x, int32_t y,
+                                               uint32_t bytes = kCodeTileBytes) {
   if (threadIdx.x == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(bar, kCodeTileBytes);
+    mbar_arrive_expect_tx(bar, bytes);
     tma_load_2d(tile, map, x, y, bar);
   }
   const bool ok = mbar_wait(bar, 0);
@@ -59,20 +60,24 @@ __device__ __forceinline__ bool load_code_tile(uint8_t* tile, uint64_t* bar, con
 }
 
 // ------------------------------------------------------------------ col (C4)
-// Lane = row.  A lane turns its row's 16-byte code chunk into eight words of
-// four FP8 bytes (elements 4k..4k+3 of that row); four neighbouring lanes then
-// transpose their 4x4 byte blocks with two shuffles so that each lane holds
-// four rows of one element and stores them as one word of the transposed tile.
-constexpr int kColPitch = 160;  // bytes per element row of the transposed tile
+// Tile: 128 rows x 128 code bytes (256 elements).  Rows are read as 128-byte
+// runs (narrower runs at the row pitch of the code matrix cost DRAM bandwidth:
+// 64-byte runs stream at ~4.1 TB/s, 128-byte runs at ~6.3 TB/s on B200).  One
+// TMA box with the 128-byte swizzle lands the tile so that a warp whose lanes
+// are 32 consecutive rows reads it without bank conflicts.  Lane = row: a lane
+// maps 4 nibbles per `prmt` through its 32-column block's table row, then four
+// neighbouring lanes transpose their 4x4 byte blocks with two shuffles so each
+// lane stores four rows of one element as one word of the transposed tile,
+// which leaves as 128-byte runs of output rows.
+constexpr int kColPitch = 160;                 // bytes per element row of the transposed tile
+constexpr uint32_t kColCodeBytes = 128 * 128;  // 16 KiB
+constexpr size_t kColSmem = 1024 + kColCodeBytes + 256 * kColPitch + 4 * 8 + 16;
 
 // 4x4 byte transpose across lanes 4m..4m+3: in, lane i holds row i's bytes for
 // elements 0..3; out, lane i holds element i's bytes for rows 0..3.
-__device__ __forceinline__ uint32_t transpose4x4(uint32_t w, uint32_t lane) {
-  const uint32_t b1 = lane & 1u, b2 = lane & 2u;
-  uint32_t o = __shfl_xor_sync(0xffffffffu, w, 2);
-  uint32_t t = b2 ? prmt(o, w, 0x7632u) : prmt(w, o, 0x5410u);
-  o = __shfl_xor_sync(0xffffffffu, t, 1);
-  return b1 ? prmt(o, t, 0x7351u) : prmt(t, o, 0x6240u);
+__device__ __forceinline__ uint32_t transpose4x4(uint32_t w, uint32_t sel1, uint32_t sel2) {
+  const uint32_t t = prmt(w, __shfl_xor_sync(0xffffffffu, w, 2), sel1);
+  return prmt(t, __shfl_xor_sync(0xffffffffu, t, 1), sel2);
 }
 
 __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant__ CUtensorMap tmap,
@@ -80,35 +85,49 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
                                                            int64_t M, int64_t Kb,
                                                            uint8_t* __restrict__ out,
                                                            float* __restrict__ scales_out) {
-  __shared__ __align__(1024) uint8_t ctile[kCodeTileBytes];
-  __shared__ __align__(16) uint8_t tr[128 * kColPitch];  // [element][row] FP8
-  __shared__ uint32_t red[4];
-  __shared__ uint64_t bar;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* ctile = smem;                                      // 128 x 128 B (128-byte swizzle)
+  uint8_t* tr = smem + kColCodeBytes;                         // [element][row] FP8
+  uint32_t* red = reinterpret_cast<uint32_t*>(tr + 256 * kColPitch);  // [4 row blocks][2 words]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(red + 8);
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int rb = warp >> 1, hh = warp & 1;  // 32-row block, 32-byte half of the tile
+  const int rb = warp >> 1, hh = warp & 1;  // 32-row block, 64-byte half of the tile
   const int64_t row0 = (int64_t)blockIdx.y * 128;
-  const int64_t cb0 = (int64_t)blockIdx.x * 64;  // first code byte of the tile
+  const int64_t cb0 = (int64_t)blockIdx.x * 128;  // first code byte of the tile
   const int64_t S = Kb / 16;
   const int r = rb * 32 + lane;
 
-  // this row's four E8M0 bytes (one per 32-column block of the tile)
-  const uint32_t sc = ld_stream_u32(scales + (row0 + r) * S + cb0 / 16);
+  // this row's eight E8M0 bytes (one per 32-column block of the tile)
+  const uint2 sc = ld_stream_v2(scales + (row0 + r) * S + cb0 / 16);
   if (hh == 0) {
-    uint32_t m = sc;
+    uint32_t m0 = sc.x, m1 = sc.y;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = vmax_u8x4(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[rb] = m;
+    for (int o = 16; o > 0; o >>= 1) {
+      m0 = vmax_u8x4(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+      m1 = vmax_u8x4(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+    }
+    if (lane == 0) {
+      red[rb * 2] = m0;
+      red[rb * 2 + 1] = m1;
+    }
   }
-  if (!load_code_tile(ctile, &bar, &tmap, (int32_t)cb0, (int32_t)row0)) return;
-  const uint32_t mx = vmax_u8x4(vmax_u8x4(red[0], red[1]), vmax_u8x4(red[2], red[3]));
+  if (!load_code_tile(ctile, bar, &tmap, (int32_t)cb0, (int32_t)row0, kColCodeBytes)) return;
+  const uint32_t mx0 = vmax_u8x4(vmax_u8x4(red[0], red[2]), vmax_u8x4(red[4], red[6]));
+  const uint32_t mx1 = vmax_u8x4(vmax_u8x4(red[1], red[3]), vmax_u8x4(red[5], red[7]));
+  // lane-dependent byte selectors of the two transpose rounds
+  const uint32_t sel1 = (lane & 2) ? 0x3276u : 0x5410u;
+  const uint32_t sel2 = (lane & 1) ? 0x3715u : 0x6240u;
   // this lane stores element (4k + (lane & 3)) for rows (lane & ~3) .. +3
   uint8_t* trl = tr + (lane & 3) * kColPitch + rb * 32 + (lane & ~3);
 
 #pragma unroll
-  for (int cc = 0; cc < 2; ++cc) {
-    const int q = 2 * hh + cc;  // 32-column block
-    const uint4 v = ld_code_chunk(ctile, r, q);
-    const uint32_t d = ((mx >> (8 * q)) & 0xFFu) - ((sc >> (8 * q)) & 0xFFu);
+  for (int cc = 0; cc < 4; ++cc) {
+    const int q = 4 * hh + cc;  // 32-column block (16 code bytes) of the tile
+    const uint4 v = *reinterpret_cast<const uint4*>(ctile + r * 128 + ((q ^ (r & 7)) << 4));
+    const uint32_t e = ((q < 4 ? sc.x : sc.y) >> (8 * (q & 3))) & 0xFFu;
+    const uint32_t d = (((q < 4 ? mx0 : mx1) >> (8 * (q & 3))) & 0xFFu) - e;
     const uint2 tb = __ldg(reinterpret_cast<const uint2*>(g_lut_col.v[d]));
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -117,20 +136,21 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
       for (int hw = 0; hw < 2; ++hw) {
         const uint32_t f4 = lut_lookup4_nosign(w[j] >> (16 * hw), tb.x, tb.y);
         const int n = q * 32 + j * 8 + hw * 4;
-        *reinterpret_cast<uint32_t*>(trl + n * kColPitch) = transpose4x4(f4, (uint32_t)lane);
+        *reinterpret_cast<uint32_t*>(trl + n * kColPitch) = transpose4x4(f4, sel1, sel2);
       }
     }
   }
   __syncthreads();
   // scales: [M/128, 2*Kb], each block scale repeated over its 32 columns
-  if (t < 128) {
-    const uint32_t wa = ((mx >> (8 * (t >> 5))) - 6u) & 0xFFu;
+  {
+    const int q = t >> 5;
+    const uint32_t wa = ((((q < 4 ? mx0 : mx1) >> (8 * (q & 3))) & 0xFFu) - 6u) & 0xFFu;
     scales_out[(row0 / 128) * (2 * Kb) + 2 * cb0 + t] = __uint_as_float(wa << 23);
   }
-  // output rows n = 2*cb0 + 0..127: 128 FP8 bytes each at columns row0..row0+127
+  // output rows n = 2*cb0 + 0..255: 128 FP8 bytes each at columns row0..row0+127
   uint8_t* ob = out + 2 * cb0 * M + row0;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < 8; ++k) {
     const int i = k * kThreads + t;
     const int n = i >> 3, part = i & 7;
     const uint4 o = *reinterpret_cast<const uint4*>(&tr[n * kColPitch + part * 16]);
@@ -391,15 +411,20 @@ extern "C" mxb_status mxb_per_token_Mxfp4ToFp8_col(const void* input, const void
   if (M == 0 || Kb == 0) return MXB_OK;
   MXB_REQUIRE(input && input_s && output_q && output_s, MXB_ERR_INVALID_ARGUMENT,
               "mxfp4_to_fp8_col: null pointer");
-  MXB_REQUIRE(aligned(input, 16) && aligned(input_s, 4) && aligned(output_q, 16),
+  MXB_REQUIRE(aligned(input, 16) && aligned(input_s, 8) && aligned(output_q, 16),
               MXB_ERR_MISALIGNED, "mxfp4_to_fp8_col: misaligned pointer");
   CUtensorMap tmap;
-  if (!make_tensor_map_2d(&tmap, input, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, Kb, Kb, 64, 128,
-                          CU_TENSOR_MAP_SWIZZLE_64B))
+  if (!make_tensor_map_2d(&tmap, input, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, Kb, Kb, 128, 128,
+                          CU_TENSOR_MAP_SWIZZLE_128B))
     return MXB_ERR_CUDA;
-  const dim3 grid((unsigned)(Kb / 64), (unsigned)(M / 128));
-  fp8_col_kernel<<<grid, kThreads, 0, to_cuda(stream)>>>(tmap, (const uint8_t*)input_s, M, Kb,
-                                                         (uint8_t*)output_q, (float*)output_s);
+  static const bool attr_ok =
+      cudaFuncSetAttribute((const void*)fp8_col_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kColSmem) == cudaSuccess;
+  MXB_REQUIRE(attr_ok, MXB_ERR_CUDA, "mxfp4_to_fp8_col: cannot reserve shared memory");
+  const dim3 grid((unsigned)(Kb / 128), (unsigned)(M / 128));
+  fp8_col_kernel<<<grid, kThreads, kColSmem, to_cuda(stream)>>>(tmap, (const uint8_t*)input_s, M,
+                                                                Kb, (uint8_t*)output_q,
+                                                                (float*)output_s);
   return launch_status("mxfp4_to_fp8_col");
 }
 
