@@ -17,7 +17,7 @@
 // one, so neither the rounding of the division nor log2f can move the ceiling;
 // -33 = ceil(log2(1e-10)) is the clamp, and eps <= 6e-10 never raises amax/6
 // above it.  The block amax is an integer max over BF16 magnitude patterns,
-// x * 2^-k is exact (two lanes per mul.rn.f32x2), and the codes come from
+// x * 2^-k is one fma.rn.f32.bf16 per value (see encode8_pairs), and the codes come from
 // Blackwell's cvt.rn.satfinite.e2m1x2.f32, whose round-to-nearest-even with
 // the sign kept on zero equals the reference's integer rounding for every
 // such product (both are checked exhaustively against the reference kernel).
@@ -91,34 +91,43 @@ __device__ __forceinline__ float amax_generic(const uint32_t (&f)[N], float init
 }
 
 // ------------------------------------------------------------ fast path
-// Exact scale exponent from the largest finite |x| pattern (see file header).
-__device__ __forceinline__ void scale_fast(uint32_t mb, uint32_t& byte, uint64_t& inv2) {
+// Exact scale exponent from the largest finite |x| pattern (see file header);
+// inv = 2^-k as a BF16 bit pattern (127 - k lies in [2, 160]: always normal).
+__device__ __forceinline__ void scale_fast(uint32_t mb, uint32_t& byte, uint32_t& inv) {
   int k = (int)(mb >> 7) - 129 + ((mb & 0x7Fu) > 0x40u ? 1 : 0);
   k = k < -33 ? -33 : k;
   byte = (uint32_t)(k + 127);
-  const uint64_t ib = (uint64_t)((uint32_t)(127 - k) << 23);
-  inv2 = (ib << 32) | ib;  // 2^-k in both f32x2 lanes
+  inv = (uint32_t)(127 - k) << 7;
 }
 
-// 8 values given as float bit patterns times 2^-k -> one code word.
-__device__ __forceinline__ uint32_t encode8_fast(const uint32_t (&f)[8], uint64_t inv2) {
+// Eight BF16 values times the BF16 power of two `inv` -> one word of eight
+// E2M1 codes (value i in nibble i).  Each product is formed by the sm_100
+// mixed-precision fma.rn.f32.bf16 (a * b + -0 in f32), which widens and scales
+// in one full-rate FMA-pipe instruction; the product of a BF16 value and a
+// power of two is exact in f32 (or rounds once below its subnormal range,
+// exactly like the reference's float multiply), and adding -0 keeps the sign
+// of zero.  kLo / kHi pick which 16-bit half of each word holds the values:
+//   encode8_pairs: words w[0..3], element order lo0, hi0, lo1, hi1, ...
+//   encode8_half<kHi>: words w[0..7], value i = half kHi of w[i].
+__device__ __forceinline__ uint32_t encode8_pairs(const uint32_t* w, uint32_t inv) {
   uint32_t r;
   asm("{\n"
-      ".reg .b64 x0, x1, x2, x3;\n"
+      ".reg .b16 l0, h0, l1, h1, l2, h2, l3, h3, s, sx;\n"
       ".reg .f32 a0, b0, a1, b1, a2, b2, a3, b3;\n"
       ".reg .b8 c0, c1, c2, c3;\n"
-      "mov.b64 x0, {%1, %2};\n"
-      "mov.b64 x1, {%3, %4};\n"
-      "mov.b64 x2, {%5, %6};\n"
-      "mov.b64 x3, {%7, %8};\n"
-      "mul.rn.f32x2 x0, x0, %9;\n"
-      "mul.rn.f32x2 x1, x1, %9;\n"
-      "mul.rn.f32x2 x2, x2, %9;\n"
-      "mul.rn.f32x2 x3, x3, %9;\n"
-      "mov.b64 {a0, b0}, x0;\n"
-      "mov.b64 {a1, b1}, x1;\n"
-      "mov.b64 {a2, b2}, x2;\n"
-      "mov.b64 {a3, b3}, x3;\n"
+      "mov.b32 {l0, h0}, %1;\n"
+      "mov.b32 {l1, h1}, %2;\n"
+      "mov.b32 {l2, h2}, %3;\n"
+      "mov.b32 {l3, h3}, %4;\n"
+      "mov.b32 {s, sx}, %5;\n"
+      "fma.rn.f32.bf16 a0, l0, s, 0f80000000;\n"
+      "fma.rn.f32.bf16 b0, h0, s, 0f80000000;\n"
+      "fma.rn.f32.bf16 a1, l1, s, 0f80000000;\n"
+      "fma.rn.f32.bf16 b1, h1, s, 0f80000000;\n"
+      "fma.rn.f32.bf16 a2, l2, s, 0f80000000;\n"
+      "fma.rn.f32.bf16 b2, h2, s, 0f80000000;\n"
+      "fma.rn.f32.bf16 a3, l3, s, 0f80000000;\n"
+      "fma.rn.f32.bf16 b3, h3, s, 0f80000000;\n"
       "cvt.rn.satfinite.e2m1x2.f32 c0, b0, a0;\n"
       "cvt.rn.satfinite.e2m1x2.f32 c1, b1, a1;\n"
       "cvt.rn.satfinite.e2m1x2.f32 c2, b2, a2;\n"
@@ -126,10 +135,49 @@ __device__ __forceinline__ uint32_t encode8_fast(const uint32_t (&f)[8], uint64_
       "mov.b32 %0, {c0, c1, c2, c3};\n"
       "}"
       : "=r"(r)
-      : "r"(f[0]), "r"(f[1]), "r"(f[2]), "r"(f[3]), "r"(f[4]), "r"(f[5]), "r"(f[6]), "r"(f[7]),
-        "l"(inv2));
+      : "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(inv));
   return r;
 }
+
+#define MXB_ENCODE8_HALF_BODY(MOVS)                                                      \
+  asm("{\n"                                                                              \
+      ".reg .b16 p0, x0, p1, x1, p2, x2, p3, x3, p4, x4, p5, x5, p6, x6, p7, x7, s, sx;\n" \
+      ".reg .f32 v0, v1, v2, v3, v4, v5, v6, v7;\n"                                      \
+      ".reg .b8 c0, c1, c2, c3;\n" MOVS                                                  \
+      "mov.b32 {s, sx}, %9;\n"                                                           \
+      "fma.rn.f32.bf16 v0, p0, s, 0f80000000;\n"                                         \
+      "fma.rn.f32.bf16 v1, p1, s, 0f80000000;\n"                                         \
+      "fma.rn.f32.bf16 v2, p2, s, 0f80000000;\n"                                         \
+      "fma.rn.f32.bf16 v3, p3, s, 0f80000000;\n"                                         \
+      "fma.rn.f32.bf16 v4, p4, s, 0f80000000;\n"                                         \
+      "fma.rn.f32.bf16 v5, p5, s, 0f80000000;\n"                                         \
+      "fma.rn.f32.bf16 v6, p6, s, 0f80000000;\n"                                         \
+      "fma.rn.f32.bf16 v7, p7, s, 0f80000000;\n"                                         \
+      "cvt.rn.satfinite.e2m1x2.f32 c0, v1, v0;\n"                                        \
+      "cvt.rn.satfinite.e2m1x2.f32 c1, v3, v2;\n"                                        \
+      "cvt.rn.satfinite.e2m1x2.f32 c2, v5, v4;\n"                                        \
+      "cvt.rn.satfinite.e2m1x2.f32 c3, v7, v6;\n"                                        \
+      "mov.b32 %0, {c0, c1, c2, c3};\n"                                                  \
+      "}"                                                                                \
+      : "=r"(r)                                                                          \
+      : "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]),     \
+        "r"(w[7]), "r"(inv))
+
+template <bool kHi>
+__device__ __forceinline__ uint32_t encode8_half(const uint32_t* w, uint32_t inv) {
+  uint32_t r;
+  if constexpr (kHi) {
+    MXB_ENCODE8_HALF_BODY("mov.b32 {x0, p0}, %1;\n mov.b32 {x1, p1}, %2;\n mov.b32 {x2, p2}, %3;\n"
+                          "mov.b32 {x3, p3}, %4;\n mov.b32 {x4, p4}, %5;\n mov.b32 {x5, p5}, %6;\n"
+                          "mov.b32 {x6, p6}, %7;\n mov.b32 {x7, p7}, %8;\n");
+  } else {
+    MXB_ENCODE8_HALF_BODY("mov.b32 {p0, x0}, %1;\n mov.b32 {p1, x1}, %2;\n mov.b32 {p2, x2}, %3;\n"
+                          "mov.b32 {p3, x3}, %4;\n mov.b32 {p4, x4}, %5;\n mov.b32 {p5, x5}, %6;\n"
+                          "mov.b32 {p6, x6}, %7;\n mov.b32 {p7, x7}, %8;\n");
+  }
+  return r;
+}
+#undef MXB_ENCODE8_HALF_BODY
 
 // Largest |x| BF16 pattern of the BF16 pairs in w; >= 0x7F80 when an Inf or
 // NaN is present (NaN reduces to 0x7FFF).
@@ -154,14 +202,10 @@ __device__ __forceinline__ void quant_block32(const uint32_t (&w)[16], const Qua
                                               uint32_t (&out)[4], uint32_t& byte) {
   const uint32_t mb = max_abs_pairs(w);
   if (kFast && mb < 0x7F80u) {
-    uint64_t inv2;
-    scale_fast(mb, byte, inv2);
+    uint32_t inv;
+    scale_fast(mb, byte, inv);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint32_t f[8];
-      unpack8(&w[4 * i], f);
-      out[i] = encode8_fast(f, inv2);
-    }
+    for (int i = 0; i < 4; ++i) out[i] = encode8_pairs(&w[4 * i], inv);
   } else {
     uint32_t fa[32];
 #pragma unroll
@@ -215,14 +259,10 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __
     mb = max(mb, __shfl_xor_sync(pair_mask, mb, 1));
     uint32_t byte, out[2];
     if (kFast && mb < 0x7F80u) {
-      uint64_t inv2;
-      scale_fast(mb, byte, inv2);
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        uint32_t f[8];
-        unpack8(&w[4 * i], f);
-        out[i] = encode8_fast(f, inv2);
-      }
+      uint32_t inv;
+      scale_fast(mb, byte, inv);
+      out[0] = encode8_pairs(&w[0], inv);
+      out[1] = encode8_pairs(&w[4], inv);
     } else {
       uint32_t f0[8], f1[8];
       unpack8(&w[0], f0);
@@ -387,16 +427,11 @@ __global__ void __launch_bounds__(kRowColThreads, 2) quant_rowcol_kernel(
         const uint32_t mb = h ? (m >> 16) : (m & 0xFFFFu);
         uint32_t out[4], byte;
         if (kFast && mb < 0x7F80u) {
-          uint64_t inv2;
-          scale_fast(mb, byte, inv2);
+          uint32_t inv;
+          scale_fast(mb, byte, inv);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t f[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              f[j] = h ? (w[8 * q + j] & 0xFFFF0000u) : (w[8 * q + j] << 16);
-            out[q] = encode8_fast(f, inv2);
-          }
+          for (int q = 0; q < 4; ++q)
+            out[q] = h ? encode8_half<true>(&w[8 * q], inv) : encode8_half<false>(&w[8 * q], inv);
         } else {
           uint32_t fa[32];
 #pragma unroll
