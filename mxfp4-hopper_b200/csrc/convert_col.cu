@@ -35,12 +35,6 @@ __device__ __forceinline__ uint32_t vmax_u8x4(uint32_t a, uint32_t b) {
   return r;
 }
 
-// 16-byte chunk c of row r of a 128 x 64-byte tile loaded with the TMA
-// 64-byte swizzle (chunk index XOR bits 7..8 of the byte offset).
-__device__ __forceinline__ uint4 ld_code_chunk(const uint8_t* tile, int r, int c) {
-  return *reinterpret_cast<const uint4*>(tile + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
-}
-
 // Loads the tile with one TMA and waits (bounded).  Returns false, for every
 // thread of the CTA, if the copy never completed.
 __device__ __forceinline__ bool load_code_tile(uint8_t* tile, uint64_t* bar, const CUtensorMap* map,
@@ -159,20 +153,213 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
 }
 
 // ------------------------------------------------------- colT / colT-split
-// Tile: 128 rows x 128 elements.  Phase 1 decodes the tile to BF16 (code x
-// E8M0 scale, exact) in shared memory, phase 2 finds each column's amax,
-// phase 3 scales, clamps and converts column pairs to FP8 into a transposed
-// staging tile (128-byte rows, 16-byte chunks XOR-swizzled by row / 2), and
-// phase 4 writes that tile out as 128-byte row runs.
-constexpr int kTPitch = 272;  // bytes per BF16 row in shared memory (256 + 16)
-
+// Persistent: each CTA walks tiles of 128 rows x 128 elements (tile = blockIdx.x
+// + i * gridDim.x, row blocks fastest so that neighbouring CTAs extend the same
+// output rows).  While it converts tile i, the TMA copy of tile i+1's codes
+// lands in the other half of a two-stage ring and tile i+1's E8M0 bytes are in
+// flight to registers, so neither load's latency is exposed.
+//
+// Thread (wc = t % 16, rg = t / 16) owns the 8 x 8 block of rows 8rg..8rg+7 and
+// columns 8wc..8wc+7 and keeps it in registers, as f32, from decode to FP8:
+//   1. one 32-bit code word per row (lanes 16..31 read their rows in the order
+//      k ^ 1 so that the two half-warps hit different bank halves), decoded and
+//      scaled by the row's E8M0 factor (decode8_scaled: exact);
+//   2. column amax over the 8 rows (three-input max of magnitudes), then across
+//      the warp's two row groups with one shuffle, then across the 8 warps
+//      through shared memory;
+//   3. per column, row pairs are scaled and converted to E4M3 (the 8 bytes of
+//      the column's 8 rows) and stored as one 8-byte chunk of the transposed
+//      staging tile, whose 8-byte chunk index is XOR-swizzled by column / 8 so
+//      that the 16 lanes of a half-warp hit 16 different bank pairs;
+//   4. the staging tile leaves as 128-byte runs of output rows.
+// The instruction mix is chosen for the SM's pipes: decoding runs on the
+// conversion unit, widening and scaling on the FMA pipe, leaving the integer
+// pipe the amax, the E4M3 conversion and the transpose.
 struct SplitArgs {
   const int32_t* m_splits;
   const int32_t* split_offsets;
   const int32_t* scale_offsets;
 };
 
-__device__ __forceinline__ int out_swz(int n, int chunk) { return n * 128 + ((chunk ^ ((n >> 1) & 7)) << 4); }
+// Position of a CTA in its tile walk: tile = (z * ns + s) * nb + b, where z is
+// the 128-column block, s the segment (always 0 without splits) and b the
+// 128-row block within it.  Advancing by gridDim.x tiles is a carry-add of the
+// step's own (z, s, b) digits, so the walk needs no division after the start.
+struct ColTWalk {
+  int64_t z;
+  int s, b;
+};
+
+__device__ __forceinline__ ColTWalk colT_digits(int64_t idx, int ns, int nb) {
+  ColTWalk w;
+  const int64_t sb = (int64_t)ns * nb;
+  w.z = idx / sb;
+  const int64_t r = idx - w.z * sb;
+  w.s = (int)(r / nb);
+  w.b = (int)(r - (int64_t)w.s * nb);
+  return w;
+}
+
+__device__ __forceinline__ void colT_advance(ColTWalk& w, const ColTWalk& step, int ns, int nb) {
+  w.z += step.z;
+  w.s += step.s;
+  w.b += step.b;
+  if (w.b >= nb) {
+    w.b -= nb;
+    ++w.s;
+  }
+  if (w.s >= ns) {
+    w.s -= ns;
+    ++w.z;
+  }
+}
+
+// Where one 128 x 128 tile reads and writes.
+struct ColTTile {
+  int64_t row_start, out_base, out_pitch, scale_row, col0;
+  int rows, cols;
+};
+
+// Tile at walk position w; false if it lies past the end of its segment.
+template <bool kSplit>
+__device__ __forceinline__ bool colT_tile(const ColTWalk& w, int64_t M, int64_t N,
+                                          const SplitArgs& sa, ColTTile& g) {
+  g.col0 = w.z * 128;
+  g.cols = (int)min((int64_t)128, N - g.col0);
+  if (kSplit) {
+    const int64_t mi = sa.m_splits[w.s];
+    if ((int64_t)w.b * 128 >= mi) return false;
+    const int64_t o = sa.split_offsets[w.s];
+    g.row_start = o + (int64_t)w.b * 128;
+    g.rows = (int)min((int64_t)128, mi - (int64_t)w.b * 128);
+    g.out_base = o * N + (int64_t)w.b * 128;  // + n * mi + local row
+    g.out_pitch = mi;
+    g.scale_row = sa.scale_offsets[w.s] + w.b;
+  } else {
+    g.row_start = (int64_t)w.b * 128;
+    g.rows = (int)min((int64_t)128, M - g.row_start);
+    g.out_base = g.row_start;
+    g.out_pitch = M;
+    g.scale_row = w.b;
+  }
+  return true;
+}
+
+// Advances w to this CTA's next non-empty tile; false when the walk is over.
+template <bool kSplit>
+__device__ __forceinline__ bool colT_next(ColTWalk& w, const ColTWalk& step, int64_t zt, int ns,
+                                          int nb, int64_t M, int64_t N, const SplitArgs& sa,
+                                          ColTTile& g) {
+  for (;;) {
+    colT_advance(w, step, ns, nb);
+    if (w.z >= zt) return false;
+    if (colT_tile<kSplit>(w, M, N, sa, g)) return true;
+  }
+}
+
+// Row r's four E8M0 bytes of a tile, loaded raw so that the load's latency
+// stays hidden until colT_factors consumes them at the end of the tile.
+__device__ __forceinline__ uint32_t colT_scale_word(const uint8_t* scales, int64_t S,
+                                                    const ColTTile& g, int r) {
+  uint32_t sc = 0;
+  if (r < g.rows) {
+    const uint8_t* sp = scales + (g.row_start + r) * S + g.col0 / 32;
+    if (g.cols == 128 && (reinterpret_cast<uintptr_t>(sp) & 3) == 0) {
+      sc = ld_stream_u32(sp);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (q * 32 < g.cols) sc |= (uint32_t)ld_stream_u8(sp + q) << (8 * q);
+    }
+  }
+  return sc;
+}
+
+// Stores row r's four E8M0 factors of a tile as float bit patterns (e << 23:
+// e = 0 reads 0, e = 255 reads Inf, as the reference's BF16 reading does; 1.0
+// past the tile's edges) into fac[q * 128 + r]; true if a factor is Inf.
+__device__ __forceinline__ bool colT_factors(uint32_t sc, const ColTTile& g, int r, uint32_t* fac) {
+  bool special = false;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t e = (sc >> (8 * q)) & 0xFFu;
+    const bool in = r < g.rows && q * 32 < g.cols;
+    fac[q * 128 + r] = in ? e << 23 : 0x3F800000u;
+    special = special || (in && e == 255u);
+  }
+  return special;
+}
+
+// Eight E2M1 codes (one code word: value i in nibble i) times the E8M0
+// factor sf -> eight floats, exactly the reference's BF16 products widened:
+// Blackwell's cvt.rn.f16x2.e2m1x2 decodes a code byte, the sm_100
+// mixed-precision add.rn.f32.f16 widens each half (adding -0 keeps the sign of
+// zero), and mul.rn.f32x2 scales by the power of two sf (exact; sf = 0 gives
+// zeros, sf = Inf gives Inf or the NaN of 0 * Inf, as the BF16 product does).
+__device__ __forceinline__ void decode8_scaled(uint32_t w, float sf, float (&o)[8]) {
+  asm("{\n"
+      ".reg .b8 b0, b1, b2, b3;\n"
+      ".reg .b32 h0, h1, h2, h3;\n"
+      ".reg .b16 p0, p1, p2, p3, p4, p5, p6, p7;\n"
+      ".reg .f32 f0, f1, f2, f3, f4, f5, f6, f7;\n"
+      ".reg .b64 x0, x1, x2, x3, s2;\n"
+      "mov.b32 {b0, b1, b2, b3}, %8;\n"
+      "cvt.rn.f16x2.e2m1x2 h0, b0;\n"
+      "cvt.rn.f16x2.e2m1x2 h1, b1;\n"
+      "cvt.rn.f16x2.e2m1x2 h2, b2;\n"
+      "cvt.rn.f16x2.e2m1x2 h3, b3;\n"
+      "mov.b32 {p0, p1}, h0;\n"
+      "mov.b32 {p2, p3}, h1;\n"
+      "mov.b32 {p4, p5}, h2;\n"
+      "mov.b32 {p6, p7}, h3;\n"
+      "add.rn.f32.f16 f0, p0, 0f80000000;\n"
+      "add.rn.f32.f16 f1, p1, 0f80000000;\n"
+      "add.rn.f32.f16 f2, p2, 0f80000000;\n"
+      "add.rn.f32.f16 f3, p3, 0f80000000;\n"
+      "add.rn.f32.f16 f4, p4, 0f80000000;\n"
+      "add.rn.f32.f16 f5, p5, 0f80000000;\n"
+      "add.rn.f32.f16 f6, p6, 0f80000000;\n"
+      "add.rn.f32.f16 f7, p7, 0f80000000;\n"
+      "mov.b64 s2, {%9, %9};\n"
+      "mov.b64 x0, {f0, f1};\n"
+      "mov.b64 x1, {f2, f3};\n"
+      "mov.b64 x2, {f4, f5};\n"
+      "mov.b64 x3, {f6, f7};\n"
+      "mul.rn.f32x2 x0, x0, s2;\n"
+      "mul.rn.f32x2 x1, x1, s2;\n"
+      "mul.rn.f32x2 x2, x2, s2;\n"
+      "mul.rn.f32x2 x3, x3, s2;\n"
+      "mov.b64 {%0, %1}, x0;\n"
+      "mov.b64 {%2, %3}, x1;\n"
+      "mov.b64 {%4, %5}, x2;\n"
+      "mov.b64 {%6, %7}, x3;\n"
+      "}"
+      : "=f"(o[0]), "=f"(o[1]), "=f"(o[2]), "=f"(o[3]), "=f"(o[4]), "=f"(o[5]), "=f"(o[6]),
+        "=f"(o[7])
+      : "r"(w), "f"(sf));
+}
+
+// Two floats per cvt: four E4M3 bytes of (a0, a1, b0, b1), RNE, saturating.
+__device__ __forceinline__ uint32_t cvt_e4m3x4(float a0, float a1, float b0, float b1) {
+  uint32_t r;
+  asm("{\n .reg .b16 lo, hi;\n"
+      " cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n"
+      " cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n"
+      " mov.b32 %0, {lo, hi};\n}"
+      : "=r"(r)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+  return r;
+}
+
+// max(|a|, |b|, |c|), NaN inputs ignored (sm_100 three-input max).
+__device__ __forceinline__ float max3_abs(float a, float b, float c) {
+  float r;
+  asm("max.abs.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+constexpr int kColTStages = 2;
+constexpr uint32_t kColTCodeBytes = 128 * 64;  // 128 rows x 64 code bytes, unswizzled
 
 template <bool kSplit>
 __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constant__ CUtensorMap tmap,
@@ -180,210 +367,201 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
                                                             int64_t M, int64_t N, float eps,
                                                             uint8_t* __restrict__ out,
                                                             float* __restrict__ scales_out,
-                                                            SplitArgs sa) {
+                                                            SplitArgs sa, int ns, int nb,
+                                                            int64_t zt) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
-  uint8_t* ctile = smem;                                // 8 KiB codes (64-byte swizzle)
-  uint8_t* tile = smem + kCodeTileBytes;                // 128 x 272 B BF16
-  uint8_t* otile = tile + 128 * kTPitch;                // 128 x 128 B FP8 (swizzled)
-  uint32_t* part_max = reinterpret_cast<uint32_t*>(otile + 128 * 128);  // [4][128]
-  float* col_qs = reinterpret_cast<float*>(part_max + 4 * 128);         // [128]
-  uint32_t* col_clamp = reinterpret_cast<uint32_t*>(col_qs + 128);       // [128]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(col_clamp + 128);
-  int* has_special = reinterpret_cast<int*>(bar + 1);
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
+                                             ~uintptr_t(127));
+  uint8_t* ctiles = smem;                                  // 2 x [128 rows][64 B] codes
+  uint8_t* otile = ctiles + kColTStages * kColTCodeBytes;  // [128 cols][16 x 8 B] FP8, swizzled
+  uint32_t* part = reinterpret_cast<uint32_t*>(otile + 128 * 128);  // [8 warps][128 cols]
+  float* col_qs = reinterpret_cast<float*>(part + 8 * 128);         // [128]
+  uint8_t* col_clamp = reinterpret_cast<uint8_t*>(col_qs + 128);    // [128]
+  uint32_t* fac = reinterpret_cast<uint32_t*>(col_clamp + 128);     // 2 x [4 blocks][128 rows]
+  uint64_t* full = reinterpret_cast<uint64_t*>(fac + 2 * 512);      // [2]
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-
-  // tile geometry
-  int64_t row_start, rows, out_base, out_pitch, scale_row;
-  if (kSplit) {
-    const int s = blockIdx.x;
-    const int64_t mi = sa.m_splits[s];
-    const int64_t b = blockIdx.y;
-    if (b * 128 >= mi) return;
-    const int64_t o = sa.split_offsets[s];
-    row_start = o + b * 128;
-    rows = min((int64_t)128, mi - b * 128);
-    out_base = o * N + b * 128;  // + n * mi + local row
-    out_pitch = mi;
-    scale_row = sa.scale_offsets[s] + b;
-  } else {
-    row_start = (int64_t)blockIdx.x * 128;
-    rows = min((int64_t)128, M - row_start);
-    out_base = row_start;
-    out_pitch = M;
-    scale_row = blockIdx.x;
-  }
-  const int64_t col0 = (int64_t)blockIdx.z * 128;
-  const int64_t cols = min((int64_t)128, N - col0);
+  const int wc = t & 15, rg = t >> 4;
+  const uint32_t up = (uint32_t)(t >> 4) & 1u;
   const int64_t S = N / 32;
-  if (t == 0) *has_special = 0;
 
-  // this thread's row (phase 1): lane = row within a 32-row block, warp pair = half
-  const int rb = warp >> 1, hh = warp & 1, r = rb * 32 + lane;
-  uint32_t sc = 0;
-  if (r < rows) {
-    const uint8_t* sp = scales + (row_start + r) * S + col0 / 32;
-    if (cols == 128 && (reinterpret_cast<uintptr_t>(sp) & 3) == 0) {
-      sc = ld_stream_u32(sp);  // the tile's four E8M0 bytes of this row at once
-    } else {
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (q * 32 < cols) sc |= (uint32_t)ld_stream_u8(sp + q) << (8 * q);
-    }
+  const ColTWalk step = colT_digits(gridDim.x, ns, nb);
+  ColTWalk w = colT_digits(blockIdx.x, ns, nb);
+  ColTTile g;
+  if (w.z >= zt) return;
+  if (!colT_tile<kSplit>(w, M, N, sa, g) && !colT_next<kSplit>(w, step, zt, ns, nb, M, N, sa, g))
+    return;
+  bool special_next = false;  // an Inf factor in the tile whose factors this thread loaded
+  if (t == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&full[0], kColTCodeBytes);
+    tma_load_2d(ctiles, &tmap, (int32_t)(g.col0 / 2), (int32_t)g.row_start, &full[0]);
   }
-  if (!load_code_tile(ctile, bar, &tmap, (int32_t)(col0 / 2), (int32_t)row_start)) return;
+  if (t < 128) special_next = colT_factors(colT_scale_word(scales, S, g, t), g, t, fac);
+  __syncthreads();
 
-  // ---- phase 1: decode two 32-element blocks of row r
-#pragma unroll
-  for (int cc = 0; cc < 2; ++cc) {
-    const int q = 2 * hh + cc;
-    uint32_t o[16];
-    if (r < rows && q * 32 < cols) {
-      const uint4 c = ld_code_chunk(ctile, r, q);
-      const uint32_t e = (sc >> (8 * q)) & 0xFFu;
-      const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        e2m1x4_to_bf16x4(w[j], o[4 * j], o[4 * j + 1]);
-        e2m1x4_to_bf16x4(w[j] >> 16, o[4 * j + 2], o[4 * j + 3]);
+  int issued = 1;  // code tiles requested so far (tile i uses stage i & 1)
+  for (int i = 0;; ++i) {
+    const bool special_cur = special_next;
+    // ---- prefetch tile i+1: its codes into the other stage, its factors into registers
+    ColTWalk wn = w;
+    ColTTile gn;
+    const bool has_next = colT_next<kSplit>(wn, step, zt, ns, nb, M, N, sa, gn);
+    if (has_next) {
+      // the other stage was last read in tile i-1's step 1, which every thread has left
+      if (t == 0) {
+        uint64_t* bar = &full[(i + 1) & 1];
+        mbar_arrive_expect_tx(bar, kColTCodeBytes);
+        tma_load_2d(ctiles + ((i + 1) & 1) * kColTCodeBytes, &tmap, (int32_t)(gn.col0 / 2),
+                    (int32_t)gn.row_start, bar);
       }
-      if (e - 2u <= 252u) {
-        const uint32_t s2 = (e << 7) | (e << 23);
+      ++issued;
+    }
+    const uint32_t sc_next = (has_next && t < 128) ? colT_scale_word(scales, S, gn, t) : 0u;
+    const bool ok = mbar_wait(&full[i & 1], (uint32_t)(i >> 1) & 1u);
+    if (__syncthreads_or(!ok)) break;  // a tile never arrived: stop together
+
+    // ---- 1. codes and factors of this thread's 8 x 8 block -> f32 values
+    const int row_base = rg * 8;
+    uint32_t cw[8];
+    {
+      const uint32_t* ct = reinterpret_cast<const uint32_t*>(ctiles + (i & 1) * kColTCodeBytes) +
+                           row_base * 16 + wc;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) o[j] = mul_bf16x2(o[j], s2);
+      for (int k = 0; k < 8; ++k) cw[k] = ct[(k ^ (int)up) * 16];
+#pragma unroll
+      for (int k = 0; k < 8; k += 2) {  // undo the k ^ 1 read order
+        const uint32_t a = cw[k], b = cw[k + 1];
+        cw[k] = up ? b : a;
+        cw[k + 1] = up ? a : b;
+      }
+    }
+    const uint4* fp = reinterpret_cast<const uint4*>(fac + (i & 1) * 512 + (wc >> 2) * 128 + row_base);
+    const uint4 fa = fp[0], fb = fp[1];
+    const uint32_t fr[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
+    float v[8][8];  // [row][column]
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      // rows of the next segment that share this tile read as zeros (past the
+      // tensor's last row the copy itself fills zeros)
+      const uint32_t c = (kSplit && row_base + k >= g.rows) ? 0u : cw[k];
+      decode8_scaled(c, __uint_as_float(fr[k]), v[k]);
+    }
+
+    // ---- 2. column amax, starting from 0 so that all-NaN columns read 0, as
+    // the reference's fmaxf loop does
+    uint32_t am[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      float m = max3_abs(0.0f, v[0][c], v[1][c]);
+      m = max3_abs(m, v[2][c], v[3][c]);
+      m = max3_abs(m, v[4][c], v[5][c]);
+      m = max3_abs(m, v[6][c], v[7][c]);
+      am[c] = __float_as_uint(m);  // a magnitude: integer order is float order
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) am[c] = max(am[c], __shfl_xor_sync(0xffffffffu, am[c], 16));
+    if (lane < 16) {
+      uint4* pw = reinterpret_cast<uint4*>(part + warp * 128 + wc * 8);
+      pw[0] = make_uint4(am[0], am[1], am[2], am[3]);
+      pw[1] = make_uint4(am[4], am[5], am[6], am[7]);
+    }
+    const bool tile_special = __syncthreads_or(special_cur);
+    if (t < 128) {
+      uint32_t mb = part[t];
+#pragma unroll
+      for (int j = 1; j < 8; ++j) mb = max(mb, part[j * 128 + t]);
+      const float mxv = __uint_as_float(mb);
+      float qs;
+      if (!kSplit) {
+        const float amax = fmaxf(eps, mxv);
+        if (t < g.cols) scales_out[g.scale_row * N + g.col0 + t] = amax / 448.0f;
+        qs = (amax > 1e-9f) ? (448.0f / amax) : 0.0f;
       } else {
-        // zero / subnormal / Inf scales: float product, exact or Inf/NaN
-        const float s = e8m0_to_f(e);
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          o[j] = cvt_bf16x2(bf16lo_to_f(o[j]) * s, bf16hi_to_f(o[j]) * s);
-        if (e == 255u) *has_special = 1;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) o[j] = 0u;
-    }
-    uint4* dst = reinterpret_cast<uint4*>(tile + r * kTPitch + q * 64);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-  }
-  __syncthreads();
-
-  // ---- phase 2: column amax (thread = column pair x 32-row quarter)
-  {
-    const int cp = ((warp & 1) << 5) | lane, rq = warp >> 1;
-    const uint32_t* col = reinterpret_cast<const uint32_t*>(tile + rq * 32 * kTPitch) + cp;
-    if (*has_special == 0) {
-      uint32_t w[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) w[i] = col[i * (kTPitch / 4)];
-      const uint32_t m = absmax_tree<32>(w) & 0x7FFF7FFFu;
-      part_max[rq * 128 + 2 * cp] = (m & 0xFFFFu) << 16;
-      part_max[rq * 128 + 2 * cp + 1] = m & 0xFFFF0000u;
-    } else {
-      float a0 = 0.0f, a1 = 0.0f;  // fmaxf ignores NaN, as the reference's loop does
-      for (int i = 0; i < 32; ++i) {
-        const uint32_t w = col[i * (kTPitch / 4)];
-        a0 = fmaxf(a0, fabsf(bf16lo_to_f(w)));
-        a1 = fmaxf(a1, fabsf(bf16hi_to_f(w)));
-      }
-      part_max[rq * 128 + 2 * cp] = __float_as_uint(a0);
-      part_max[rq * 128 + 2 * cp + 1] = __float_as_uint(a1);
-    }
-  }
-  __syncthreads();
-  if (t < 128) {
-    // magnitudes are non-negative floats, so integer order is float order
-    const uint32_t mb = max(max(part_max[t], part_max[128 + t]),
-                            max(part_max[256 + t], part_max[384 + t]));
-    const float mxv = __uint_as_float(mb);
-    float qs;
-    if (!kSplit) {
-      const float amax = fmaxf(eps, mxv);
-      if (t < cols) scales_out[scale_row * N + col0 + t] = amax / 448.0f;
-      qs = (amax > 1e-9f) ? (448.0f / amax) : 0.0f;
-    } else {
-      const float amax = mxv;  // initialised to 0 on the split path
-      float s;
-      if (amax <= eps) {
-        s = 1.0f;
-      } else {
-        const uint32_t rbits = __float_as_uint(amax / 448.0f);
-        uint32_t ex = (rbits >> 23) & 0xFFu;
-        if (rbits & 0x7FFFFFu) ex += 1u;
-        s = (float)(1.0 / (double)__uint_as_float(ex << 23));
-      }
-      if (t < cols) scales_out[scale_row * N + col0 + t] = 1.0f / s;
-      qs = s;
-    }
-    col_qs[t] = qs;
-    // NaN products are possible only with an Inf amax or an E8M0 byte of 255
-    col_clamp[t] = (mb >= 0x7F800000u || *has_special) ? 1u : 0u;
-  }
-  __syncthreads();
-
-  // ---- phase 3: column pair x 16-row chunk -> two 16-byte runs of the staging tile.
-  // With a finite amax every |v * qs| is at most 448 (1 + 2^-23), which the
-  // saturating conversion maps exactly as clamp-then-convert does (true for
-  // every finite value), so the clamp is applied only where a NaN can occur:
-  // columns with an Inf amax (v * 0) and tiles holding an E8M0 byte of 255
-  // (0 * Inf); the reference clamps NaN to -448.
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int cp = ((warp & 1) << 5) | lane;
-    const int chunk = (warp >> 1) + 4 * k;  // 0..7
-    const uint32_t* col = reinterpret_cast<const uint32_t*>(tile + chunk * 16 * kTPitch) + cp;
-    uint32_t w[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) w[i] = col[i * (kTPitch / 4)];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const float qs = col_qs[2 * cp + h];
-      const bool clamp = col_clamp[2 * cp + h] != 0;
-      uint32_t o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const uint32_t b0 = w[4 * j + 2 * u], b1 = w[4 * j + 2 * u + 1];
-          float q0, q1;
-          mul2_f32(h ? (b0 & 0xFFFF0000u) : (b0 << 16), h ? (b1 & 0xFFFF0000u) : (b1 << 16), qs,
-                   q0, q1);
-          if (clamp) {
-            q0 = fminf(fmaxf(q0, -448.0f), 448.0f);
-            q1 = fminf(fmaxf(q1, -448.0f), 448.0f);
-          }
-          word |= cvt_e4m3x2(q0, q1) << (16 * u);
+        const float amax = mxv;  // initialised to 0 on the split path
+        float s;
+        if (amax <= eps) {
+          s = 1.0f;
+        } else {
+          const uint32_t rbits = __float_as_uint(amax / 448.0f);
+          uint32_t ex = (rbits >> 23) & 0xFFu;
+          if (rbits & 0x7FFFFFu) ex += 1u;
+          s = (float)(1.0 / (double)__uint_as_float(ex << 23));
         }
-        o[j] = word;
+        if (t < g.cols) scales_out[g.scale_row * N + g.col0 + t] = 1.0f / s;
+        qs = s;
       }
-      *reinterpret_cast<uint4*>(otile + out_swz(2 * cp + h, chunk)) = make_uint4(o[0], o[1], o[2], o[3]);
+      col_qs[t] = qs;
+      // NaN products are possible only with an Inf amax or an E8M0 byte of 255
+      col_clamp[t] = (mb >= 0x7F800000u || tile_special) ? 1 : 0;
     }
-  }
-  __syncthreads();
+    __syncthreads();
 
-  // ---- phase 4: output rows n (128 FP8 bytes each), eight lanes per row
+    // ---- 3. scale, convert row pairs to E4M3, one 8-byte chunk per column.
+    // With a finite amax every |v * qs| is at most 448 (1 + 2^-23), which the
+    // saturating conversion maps exactly as clamp-then-convert does (true for
+    // every finite value), so the clamp is needed only where a NaN can occur:
+    // columns with an Inf amax (v * 0) and tiles holding an E8M0 byte of 255
+    // (0 * Inf); the reference clamps NaN to -448.
+    {
+      const float4 qa = *reinterpret_cast<const float4*>(col_qs + wc * 8);
+      const float4 qb = *reinterpret_cast<const float4*>(col_qs + wc * 8 + 4);
+      const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+      const uint2 cl = *reinterpret_cast<const uint2*>(col_clamp + wc * 8);
+      const bool clamp = (cl.x | cl.y) != 0u;
+      uint8_t* orow = otile + (wc * 8) * 128 + ((rg ^ wc) << 3);
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int i = k * kThreads + t;
-    const int n = i >> 3, part = i & 7;
-    if (n >= cols || part * 16 >= rows) continue;
-    const uint4 o = *reinterpret_cast<const uint4*>(otile + out_swz(n, part));
-    uint8_t* dst = out + out_base + (col0 + n) * out_pitch + part * 16;
-    const int valid = (int)min((int64_t)16, rows - part * 16);
-    if (valid == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-      st_stream_v4(dst, o);
-    } else {
-      const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
-      for (int j = 0; j < valid; ++j) dst[j] = (uint8_t)(ow[j >> 2] >> (8 * (j & 3)));
+      for (int c = 0; c < 8; ++c) {
+        float q[8];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          mul2_f32(__float_as_uint(v[2 * m][c]), __float_as_uint(v[2 * m + 1][c]), qv[c], q[2 * m],
+                   q[2 * m + 1]);
+        }
+        if (clamp) {
+#pragma unroll
+          for (int m = 0; m < 8; ++m) q[m] = fminf(fmaxf(q[m], -448.0f), 448.0f);
+        }
+        *reinterpret_cast<uint2*>(orow + c * 128) =
+            make_uint2(cvt_e4m3x4(q[0], q[1], q[2], q[3]), cvt_e4m3x4(q[4], q[5], q[6], q[7]));
+      }
     }
+    __syncthreads();
+
+    // ---- 4. output rows n (128 FP8 bytes each), eight lanes per row
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = k * kThreads + t;
+      const int n = j >> 3, p = j & 7;
+      if (n >= g.cols || p * 16 >= g.rows) continue;
+      const uint32_t x = (uint32_t)(n >> 3) & 15u;  // the column's chunk swizzle
+      uint4 o = *reinterpret_cast<const uint4*>(otile + n * 128 + ((p ^ (x >> 1)) << 4));
+      if (x & 1u) o = make_uint4(o.z, o.w, o.x, o.y);
+      uint8_t* dst = out + g.out_base + (g.col0 + n) * g.out_pitch + p * 16;
+      const int valid = min(16, g.rows - p * 16);
+      if (valid == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        st_stream_v4(dst, o);
+      } else {
+        const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+        for (int b = 0; b < valid; ++b) dst[b] = (uint8_t)(ow[b >> 2] >> (8 * (b & 3)));
+      }
+    }
+    if (!has_next) return;
+    // tile i+1's factors; that buffer was last read in tile i-1's step 1
+    if (t < 128) special_next = colT_factors(sc_next, gn, t, fac + ((i + 1) & 1) * 512);
+    w = wn;
+    g = gn;
   }
+  // Left early (tile `issued - 2` or `issued - 1` never arrived): do not exit
+  // while a requested copy may still land in this CTA's memory.
+  if (t == 0)
+    for (int j = issued >= 2 ? issued - 2 : 0; j < issued; ++j)
+      mbar_wait(&full[j & 1], (uint32_t)(j >> 1) & 1u);
 }
 
-constexpr size_t kColTSmem = 1024 + kCodeTileBytes + 128 * kTPitch + 128 * 128 + 4 * 128 * 4 +
-                             2 * 128 * 4 + 16;
+constexpr size_t kColTSmem = 128 + kColTStages * kColTCodeBytes + 128 * 128 + 8 * 128 * 4 +
+                             128 * 4 + 128 + 2 * 512 * 4 + 2 * 8;
 
 bool colT_attr() {
   static const bool ok =
@@ -440,13 +618,16 @@ extern "C" mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col(const void* input, co
   MXB_REQUIRE(aligned(input, 16), MXB_ERR_MISALIGNED, "mxfp4_to_fp8_colT: input not 16-byte aligned");
   MXB_REQUIRE(colT_attr(), MXB_ERR_CUDA, "mxfp4_to_fp8_colT: cannot reserve shared memory");
   CUtensorMap tmap;
-  if (!make_tensor_map_2d(&tmap, input, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, N / 2, N / 2, 64, 128,
-                          CU_TENSOR_MAP_SWIZZLE_64B))
+  if (!make_tensor_map_2d(&tmap, input, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, N / 2, N / 2, 64, 128))
     return MXB_ERR_CUDA;
-  const dim3 grid((unsigned)cdiv(M, 128), 1, (unsigned)cdiv(N, 128));
-  fp8_colT_kernel<false><<<grid, kThreads, kColTSmem, to_cuda(stream)>>>(
-      tmap, (const uint8_t*)input_s, M, N, eps, (uint8_t*)output_q, (float*)output_s,
-      SplitArgs{nullptr, nullptr, nullptr});
+  MXB_REQUIRE(cdiv(M, 128) <= INT32_MAX, MXB_ERR_INVALID_ARGUMENT, "mxfp4_to_fp8_colT: M too large");
+  const int nb = (int)cdiv(M, 128);
+  const int64_t zt = cdiv(N, 128), tiles = zt * nb;
+  const int ctas = persistent_ctas((const void*)fp8_colT_kernel<false>, kThreads, kColTSmem);
+  fp8_colT_kernel<false><<<(unsigned)min((int64_t)ctas, tiles), kThreads, kColTSmem,
+                           to_cuda(stream)>>>(tmap, (const uint8_t*)input_s, M, N, eps,
+                                              (uint8_t*)output_q, (float*)output_s,
+                                              SplitArgs{nullptr, nullptr, nullptr}, 1, nb, zt);
   return launch_status("mxfp4_to_fp8_colT");
 }
 
@@ -469,11 +650,15 @@ extern "C" mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit(
   MXB_REQUIRE(colT_attr(), MXB_ERR_CUDA, "mxfp4_to_fp8_colT_msplit: cannot reserve shared memory");
   CUtensorMap tmap;
   if (!make_tensor_map_2d(&tmap, input, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, total_M, N / 2, N / 2,
-                          64, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+                          64, 128))
     return MXB_ERR_CUDA;
-  const dim3 grid((unsigned)num_splits, (unsigned)cdiv(max_split_len, 128), (unsigned)cdiv(N, 128));
-  fp8_colT_kernel<true><<<grid, kThreads, kColTSmem, to_cuda(stream)>>>(
-      tmap, (const uint8_t*)input_s, total_M, N, eps, (uint8_t*)output_q, (float*)output_s,
-      SplitArgs{m_splits, split_offsets, scale_offsets});
+  const int nb = (int)cdiv(max_split_len, 128);
+  const int64_t zt = cdiv(N, 128), tiles = zt * num_splits * nb;
+  const int ctas = persistent_ctas((const void*)fp8_colT_kernel<true>, kThreads, kColTSmem);
+  fp8_colT_kernel<true><<<(unsigned)min((int64_t)ctas, tiles), kThreads, kColTSmem,
+                          to_cuda(stream)>>>(tmap, (const uint8_t*)input_s, total_M, N, eps,
+                                             (uint8_t*)output_q, (float*)output_s,
+                                             SplitArgs{m_splits, split_offsets, scale_offsets},
+                                             (int)num_splits, nb, zt);
   return launch_status("mxfp4_to_fp8_colT_msplit");
 }
