@@ -379,6 +379,7 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
   uint8_t* col_clamp = reinterpret_cast<uint8_t*>(col_qs + 128);    // [128]
   uint32_t* fac = reinterpret_cast<uint32_t*>(col_clamp + 128);     // 2 x [4 blocks][128 rows]
   uint64_t* full = reinterpret_cast<uint64_t*>(fac + 2 * 512);      // [2]
+  int* timeout_flag = reinterpret_cast<int*>(full + 2);
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int wc = t & 15, rg = t >> 4;
   const uint32_t up = (uint32_t)(t >> 4) & 1u;
@@ -392,6 +393,7 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
     return;
   bool special_next = false;  // an Inf factor in the tile whose factors this thread loaded
   if (t == 0) {
+    *timeout_flag = 0;
     mbar_init(&full[0], 1);
     mbar_init(&full[1], 1);
     fence_mbar_init();
@@ -419,8 +421,10 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
       ++issued;
     }
     const uint32_t sc_next = (has_next && t < 128) ? colT_scale_word(scales, S, gn, t) : 0u;
+    // A copy that never arrives is reported at the next barrier (the tile's
+    // values are then garbage and never stored).
     const bool ok = mbar_wait(&full[i & 1], (uint32_t)(i >> 1) & 1u);
-    if (__syncthreads_or(!ok)) break;  // a tile never arrived: stop together
+    if (!ok) *timeout_flag = 1;
 
     // ---- 1. codes and factors of this thread's 8 x 8 block -> f32 values
     const int row_base = rg * 8;
@@ -467,7 +471,8 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
       pw[0] = make_uint4(am[0], am[1], am[2], am[3]);
       pw[1] = make_uint4(am[4], am[5], am[6], am[7]);
     }
-    const bool tile_special = __syncthreads_or(special_cur);
+    const bool tile_special = __syncthreads_or(special_cur || !ok);
+    if (tile_special && *timeout_flag) break;  // a tile never arrived: stop together
     if (t < 128) {
       uint32_t mb = part[t];
 #pragma unroll
@@ -529,22 +534,38 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
     }
     __syncthreads();
 
-    // ---- 4. output rows n (128 FP8 bytes each), eight lanes per row
+    // ---- 4. output rows n (128 FP8 bytes each), eight lanes per row: thread t
+    // writes chunk p = t % 8 of rows n = 32k + t / 8 (k = 0..3), whose
+    // column swizzle x = n / 8 has x & 1 = (t / 64) & 1 and x / 2 = 2k + t / 128
+    {
+      const int p = t & 7, n0 = t >> 3;
+      uint8_t* dst = out + g.out_base + (g.col0 + n0) * g.out_pitch + p * 16;
+      const int64_t stride = 32 * g.out_pitch;
+      const bool swap = (t >> 6) & 1;
+      if (g.rows == 128 && g.cols == 128 && ((reinterpret_cast<uintptr_t>(dst) | stride) & 15) == 0) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int j = k * kThreads + t;
-      const int n = j >> 3, p = j & 7;
-      if (n >= g.cols || p * 16 >= g.rows) continue;
-      const uint32_t x = (uint32_t)(n >> 3) & 15u;  // the column's chunk swizzle
-      uint4 o = *reinterpret_cast<const uint4*>(otile + n * 128 + ((p ^ (x >> 1)) << 4));
-      if (x & 1u) o = make_uint4(o.z, o.w, o.x, o.y);
-      uint8_t* dst = out + g.out_base + (g.col0 + n) * g.out_pitch + p * 16;
-      const int valid = min(16, g.rows - p * 16);
-      if (valid == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-        st_stream_v4(dst, o);
+        for (int k = 0; k < 4; ++k) {
+          const int n = 32 * k + n0;
+          uint4 o = *reinterpret_cast<const uint4*>(otile + n * 128 + ((p ^ ((2 * k + (t >> 7)) & 7)) << 4));
+          if (swap) o = make_uint4(o.z, o.w, o.x, o.y);
+          st_stream_v4(dst + k * stride, o);
+        }
       } else {
-        const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
-        for (int b = 0; b < valid; ++b) dst[b] = (uint8_t)(ow[b >> 2] >> (8 * (b & 3)));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int n = 32 * k + n0;
+          if (n >= g.cols || p * 16 >= g.rows) continue;
+          uint4 o = *reinterpret_cast<const uint4*>(otile + n * 128 + ((p ^ ((2 * k + (t >> 7)) & 7)) << 4));
+          if (swap) o = make_uint4(o.z, o.w, o.x, o.y);
+          uint8_t* d = dst + k * stride;
+          const int valid = min(16, g.rows - p * 16);
+          if (valid == 16 && (reinterpret_cast<uintptr_t>(d) & 15) == 0) {
+            st_stream_v4(d, o);
+          } else {
+            const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+            for (int b = 0; b < valid; ++b) d[b] = (uint8_t)(ow[b >> 2] >> (8 * (b & 3)));
+          }
+        }
       }
     }
     if (!has_next) return;
@@ -561,7 +582,7 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
 }
 
 constexpr size_t kColTSmem = 128 + kColTStages * kColTCodeBytes + 128 * 128 + 8 * 128 * 4 +
-                             128 * 4 + 128 + 2 * 512 * 4 + 2 * 8;
+                             128 * 4 + 128 + 2 * 512 * 4 + 2 * 8 + 16;
 
 bool colT_attr() {
   static const bool ok =
