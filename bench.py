@@ -432,7 +432,28 @@ def time_other_ops(dev, stream, peak):
         lambda: capi.call("mxb_per_token_Mxfp4RowToBf16ToFp8Col", c.data_ptr(), sc.data_ptr(), M3,
                           2 * Kb3, f8.data_ptr(), fcs.data_ptr(), 1e-10, sh),
         M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fcs.numel() * 4)
-    del c, sc, f8, fcs
+    # colT-split: config 3's rows as 8 ragged expert segments (seeded sizes, not
+    # multiples of 128, summing to M3), the grouped-GEMM wgrad operand
+    gsz = torch.Generator().manual_seed(7)
+    wts = torch.rand(8, generator=gsz) + 0.5
+    m_splits = (wts / wts.sum() * M3).floor().to(torch.int64).tolist()
+    m_splits[-1] += M3 - sum(m_splits)
+    so, sco, acc, accs = [], [], 0, 0
+    for m in m_splits:
+        so.append(acc)
+        sco.append(accs)
+        acc += m
+        accs += (m + 127) // 128
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
+    dm, dso, dsco = i32(m_splits), i32(so), i32(sco)
+    fss = torch.empty(accs, 2 * Kb3, dtype=torch.float32, device=dev)
+    res["mxfp4_to_fp8_colT_msplit8_config3"] = timeit(
+        lambda: capi.call("mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit", c.data_ptr(),
+                          sc.data_ptr(), M3, 2 * Kb3, f8.data_ptr(), fss.data_ptr(),
+                          dm.data_ptr(), dso.data_ptr(), dsco.data_ptr(), len(m_splits),
+                          max(m_splits), 1e-10, sh),
+        M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fss.numel() * 4)
+    del c, sc, f8, fcs, fss
     # config 4 per-token FP8
     x4 = syn.config4().to(dev)
     M4, K4 = x4.shape

@@ -16,6 +16,8 @@
 // are transposed through shared memory and leave as 128-byte runs of output
 // rows, eight lanes per run.  Several CTAs per SM overlap one tile's load
 // with the others' work.
+#include <type_traits>
+
 #include "capi_util.h"
 #include "common.cuh"
 #include "fp8_lut.cuh"
@@ -218,6 +220,7 @@ __device__ __forceinline__ void colT_advance(ColTWalk& w, const ColTWalk& step, 
 struct ColTTile {
   int64_t row_start, out_base, out_pitch, scale_row, col0;
   int rows, cols;
+  bool merge_in, carry_out;  // split path: partial chunks shared with the previous / next tile
 };
 
 // Tile at walk position w; false if it lies past the end of its segment.
@@ -226,6 +229,7 @@ __device__ __forceinline__ bool colT_tile(const ColTWalk& w, int64_t M, int64_t 
                                           const SplitArgs& sa, ColTTile& g) {
   g.col0 = w.z * 128;
   g.cols = (int)min((int64_t)128, N - g.col0);
+  g.merge_in = g.carry_out = false;
   if (kSplit) {
     const int64_t mi = sa.m_splits[w.s];
     if ((int64_t)w.b * 128 >= mi) return false;
@@ -254,6 +258,80 @@ __device__ __forceinline__ bool colT_next(ColTWalk& w, const ColTWalk& step, int
     colT_advance(w, step, ns, nb);
     if (w.z >= zt) return false;
     if (colT_tile<kSplit>(w, M, N, sa, g)) return true;
+  }
+}
+
+// Split path walk.  A segment's output [N, m_i] is one contiguous block, so
+// its row segments start at n * m_i and are rarely 16-byte aligned; the
+// 16-byte memory chunk a row segment shares with the next 128-row block is
+// written once, whole, when the same CTA converts that block next.  So the
+// split path walks units of up to kUnitTiles consecutive row blocks of one
+// (segment, 128-column block): unit = (s * SS + ss) * ZT + z with z fastest
+// (neighbouring CTAs convert neighbouring columns of the same rows), ss the
+// unit's index along the segment, SS = ceil(nb / kUnitTiles) for the longest
+// segment (units past a segment's end are empty).  Partial chunks remain only
+// at unit ends.  Digits (z, ss, s) advance by the step's digits without
+// division, as in the tile walk.
+constexpr int kUnitTiles = 4;
+
+struct SplitWalk {
+  int64_t z;
+  int s, ss, bi;  // bi: tile within the unit
+};
+
+__device__ __forceinline__ SplitWalk split_digits(int64_t idx, int SS, int64_t ZT) {
+  SplitWalk w;
+  const int64_t r = idx / ZT;
+  w.z = idx - r * ZT;
+  w.s = (int)(r / SS);
+  w.ss = (int)(r - (int64_t)w.s * SS);
+  w.bi = 0;
+  return w;
+}
+
+// Tile (s, z, b = kUnitTiles * ss + bi) of the split path; false past the segment's end.
+__device__ __forceinline__ bool split_tile(const SplitWalk& w, int64_t N, const SplitArgs& sa,
+                                           ColTTile& g) {
+  const int64_t mi = sa.m_splits[w.s];
+  const int64_t b = (int64_t)w.ss * kUnitTiles + w.bi;
+  if (b * 128 >= mi) return false;
+  const int64_t o = sa.split_offsets[w.s];
+  g.col0 = w.z * 128;
+  g.cols = (int)min((int64_t)128, N - g.col0);
+  g.row_start = o + b * 128;
+  g.rows = (int)min((int64_t)128, mi - b * 128);
+  g.out_base = o * N + b * 128;  // + n * mi + local row
+  g.out_pitch = mi;
+  g.scale_row = sa.scale_offsets[w.s] + b;
+  g.merge_in = w.bi > 0;
+  g.carry_out = w.bi + 1 < kUnitTiles && (b + 1) * 128 < mi;
+  return true;
+}
+
+// The CTA's next tile: the next block of the unit, else the first tile of its
+// next non-empty unit; false when the walk is over.
+__device__ __forceinline__ bool split_next(SplitWalk& w, const SplitWalk& step, int ns, int SS,
+                                           int64_t ZT, int64_t N, const SplitArgs& sa,
+                                           ColTTile& g) {
+  if (g.carry_out) {
+    ++w.bi;
+    return split_tile(w, N, sa, g);
+  }
+  for (;;) {
+    w.bi = 0;
+    w.z += step.z;
+    w.ss += step.ss;
+    w.s += step.s;
+    if (w.z >= ZT) {
+      w.z -= ZT;
+      ++w.ss;
+    }
+    if (w.ss >= SS) {
+      w.ss -= SS;
+      ++w.s;
+    }
+    if (w.s >= ns) return false;
+    if (split_tile(w, N, sa, g)) return true;
   }
 }
 
@@ -361,6 +439,123 @@ __device__ __forceinline__ float max3_abs(float a, float b, float c) {
 constexpr int kColTStages = 2;
 constexpr uint32_t kColTCodeBytes = 128 * 64;  // 128 rows x 64 code bytes, unswizzled
 
+// Stores bytes [lo, hi) of the 16-byte value v at the 16-byte aligned address
+// b, as naturally aligned pieces: pieces of 1, 2, 4, 8 bytes bring the start
+// up to 16-byte alignment, then pieces of 8, 4, 2, 1 bytes cover the rest.
+__device__ __forceinline__ void st_piece(uint8_t* b, uint64_t w0, uint64_t w1, int pos, int sz) {
+  const uint64_t piece = pos < 8 ? (w0 >> (8 * pos)) : (w1 >> (8 * (pos - 8)));
+  if (sz == 8) {
+    asm volatile("st.global.cs.u64 [%0], %1;" ::"l"(b + pos), "l"(piece) : "memory");
+  } else if (sz == 4) {
+    st_stream_u32(b + pos, (uint32_t)piece);
+  } else if (sz == 2) {
+    asm volatile("st.global.cs.u16 [%0], %1;" ::"l"(b + pos), "h"((uint16_t)piece) : "memory");
+  } else {
+    st_stream_u8(b + pos, (uint32_t)piece & 0xFFu);
+  }
+}
+
+__device__ __forceinline__ void store_bytes16(uint8_t* b, uint4 v, int lo, int hi) {
+  const uint64_t w0 = ((uint64_t)v.y << 32) | v.x, w1 = ((uint64_t)v.w << 32) | v.z;
+  int pos = lo;
+#pragma unroll
+  for (int sz = 1; sz <= 8; sz <<= 1) {
+    if ((pos & sz) && pos + sz <= hi) {
+      st_piece(b, w0, w1, pos, sz);
+      pos += sz;
+    }
+  }
+#pragma unroll
+  for (int sz = 8; sz >= 1; sz >>= 1) {
+    if (pos + sz <= hi) {
+      st_piece(b, w0, w1, pos, sz);
+      pos += sz;
+    }
+  }
+}
+
+// Bytes 0 .. a-1 from c, bytes a .. 15 from o.
+__device__ __forceinline__ uint4 blend16(uint4 c, uint4 o, int a) {
+  const uint32_t cw[4] = {c.x, c.y, c.z, c.w}, ow[4] = {o.x, o.y, o.z, o.w};
+  uint32_t r[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int k = a - 4 * i;  // bytes of word i taken from c
+    const uint32_t m = k >= 4 ? 0xFFFFFFFFu : (k <= 0 ? 0u : (1u << (8 * k)) - 1u);
+    r[i] = (cw[i] & m) | (ow[i] & ~m);
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+// Writes an output row segment of `len` bytes starting at `row`, for any
+// alignment of `row` (a segment of the split path starts at n * m_i); called
+// by the 8 lanes of a row group, lane p holding data chunk p (bytes 16p..16p+15)
+// in d, with prev = chunk (p-1) mod 8 from the neighbouring lane.  The segment
+// is written as the 16-byte aligned chunks of memory it covers: memory chunk m
+// holds data bytes 16m - a .. 16m - a + 15 (a = row % 16), the top a bytes of
+// data chunk m-1 followed by the low 16 - a bytes of chunk m, which lane m
+// builds with funnel shifts over the window of words (prev, d).  Lane 0's
+// window (chunk 7, chunk 0) serves both partial chunks: memory chunk 0 (data
+// bytes 0 .. 15 - a) and memory chunk 8 (data bytes 128 - a .. 127).  Memory
+// chunk 8 is memory chunk 0 of the next 128-row block: with carry_out it is
+// kept in *carry instead of stored, and with merge_in this block's chunk 0 is
+// completed from *carry and stored whole.  Other partial chunks are written
+// in naturally aligned pieces, so neighbouring segments' bytes are never
+// touched.
+__device__ __forceinline__ void store_row_chunk(uint8_t* row, int p, uint4 d, uint4 prev, int len,
+                                                bool merge_in, bool carry_out, uint4* carry) {
+  const uintptr_t A = reinterpret_cast<uintptr_t>(row);
+  const int a = (int)(A & 15);
+  uint8_t* base = row - a;  // 16-byte aligned
+  uint4 o = d;
+  if (a != 0) {
+    // out word i = bytes 16 - a + 4i .. + 3 of W = (prev, d): words W[qs + i],
+    // W[qs + i + 1] funnel-shifted by rs bytes, qs = (16 - a) / 4, rs = (16 - a) % 4
+    const int sft = 16 - a, qs = sft >> 2, rs = sft & 3;
+    const uint32_t W[8] = {prev.x, prev.y, prev.z, prev.w, d.x, d.y, d.z, d.w};
+    uint32_t X[5];
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+      const uint32_t lo2 = (qs & 1) ? W[k + 1] : W[k];
+      const uint32_t hi2 = (qs & 1) ? W[k + 3] : W[k + 2];
+      X[k] = (qs & 2) ? hi2 : lo2;
+    }
+    o.x = __funnelshift_r(X[0], X[1], 8 * rs);
+    o.y = __funnelshift_r(X[1], X[2], 8 * rs);
+    o.z = __funnelshift_r(X[2], X[3], 8 * rs);
+    o.w = __funnelshift_r(X[3], X[4], 8 * rs);
+  }
+  if (p != 0) {
+    // memory chunk p covers data bytes [16p - a, 16p - a + 16) clipped to [0, len)
+    const int hi = min(16, len + a - 16 * p);
+    if (hi == 16) {
+      st_stream_v4(base + 16 * p, o);
+    } else if (hi > 0) {
+      store_bytes16(base + 16 * p, o, 0, hi);
+    }
+    return;
+  }
+  // lane 0: memory chunk 0, bytes [a, min(16, len + a)) of this block
+  {
+    const int hi = min(16, len + a);
+    const uint4 v = (merge_in && a != 0) ? blend16(*carry, o, a) : o;
+    const int lo = (merge_in || a == 0) ? 0 : a;
+    if (lo == 0 && hi == 16) {
+      st_stream_v4(base, v);
+    } else {
+      store_bytes16(base, v, lo, hi);
+    }
+  }
+  // memory chunk 8, bytes [0, a) (data 128 - a .. 127), if the block is full
+  if (a != 0 && len == 128) {
+    if (carry_out) {
+      *carry = o;
+    } else {
+      store_bytes16(base + 128, o, 0, a);
+    }
+  }
+}
+
 template <bool kSplit>
 __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constant__ CUtensorMap tmap,
                                                             const uint8_t* __restrict__ scales,
@@ -380,17 +575,32 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
   uint32_t* fac = reinterpret_cast<uint32_t*>(col_clamp + 128);     // 2 x [4 blocks][128 rows]
   uint64_t* full = reinterpret_cast<uint64_t*>(fac + 2 * 512);      // [2]
   int* timeout_flag = reinterpret_cast<int*>(full + 2);
+  uint4* carry = reinterpret_cast<uint4*>(full + 4);                 // [128 output rows]
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int wc = t & 15, rg = t >> 4;
   const uint32_t up = (uint32_t)(t >> 4) & 1u;
   const int64_t S = N / 32;
 
-  const ColTWalk step = colT_digits(gridDim.x, ns, nb);
-  ColTWalk w = colT_digits(blockIdx.x, ns, nb);
+  // walk: tiles of the column/row-block grid, or units of a segment on the
+  // split path (nb is then the number of units along the longest segment)
+  using Walk = std::conditional_t<kSplit, SplitWalk, ColTWalk>;
+  Walk step, w;
   ColTTile g;
-  if (w.z >= zt) return;
-  if (!colT_tile<kSplit>(w, M, N, sa, g) && !colT_next<kSplit>(w, step, zt, ns, nb, M, N, sa, g))
-    return;
+  if constexpr (kSplit) {
+    step = split_digits(gridDim.x, nb, zt);
+    w = split_digits(blockIdx.x, nb, zt);
+    if (w.s >= ns) return;
+    if (!split_tile(w, N, sa, g)) {
+      g.carry_out = false;
+      if (!split_next(w, step, ns, nb, zt, N, sa, g)) return;
+    }
+  } else {
+    step = colT_digits(gridDim.x, ns, nb);
+    w = colT_digits(blockIdx.x, ns, nb);
+    if (w.z >= zt) return;
+    if (!colT_tile<false>(w, M, N, sa, g) && !colT_next<false>(w, step, zt, ns, nb, M, N, sa, g))
+      return;
+  }
   bool special_next = false;  // an Inf factor in the tile whose factors this thread loaded
   if (t == 0) {
     *timeout_flag = 0;
@@ -407,9 +617,14 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
   for (int i = 0;; ++i) {
     const bool special_cur = special_next;
     // ---- prefetch tile i+1: its codes into the other stage, its factors into registers
-    ColTWalk wn = w;
-    ColTTile gn;
-    const bool has_next = colT_next<kSplit>(wn, step, zt, ns, nb, M, N, sa, gn);
+    Walk wn = w;
+    ColTTile gn = g;
+    bool has_next;
+    if constexpr (kSplit) {
+      has_next = split_next(wn, step, ns, nb, zt, N, sa, gn);
+    } else {
+      has_next = colT_next<false>(wn, step, zt, ns, nb, M, N, sa, gn);
+    }
     if (has_next) {
       // the other stage was last read in tile i-1's step 1, which every thread has left
       if (t == 0) {
@@ -542,7 +757,10 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
       uint8_t* dst = out + g.out_base + (g.col0 + n0) * g.out_pitch + p * 16;
       const int64_t stride = 32 * g.out_pitch;
       const bool swap = (t >> 6) & 1;
-      if (g.rows == 128 && g.cols == 128 && ((reinterpret_cast<uintptr_t>(dst) | stride) & 15) == 0) {
+      // block-uniform: full tile, tile origin and row pitch 16-byte aligned (the
+      // other path shuffles across lanes and must be taken by whole warps)
+      const uintptr_t origin = reinterpret_cast<uintptr_t>(out + g.out_base + g.col0 * g.out_pitch);
+      if (g.rows == 128 && g.cols == 128 && ((origin | (uintptr_t)g.out_pitch) & 15) == 0) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int n = 32 * k + n0;
@@ -554,17 +772,16 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int n = 32 * k + n0;
-          if (n >= g.cols || p * 16 >= g.rows) continue;
           uint4 o = *reinterpret_cast<const uint4*>(otile + n * 128 + ((p ^ ((2 * k + (t >> 7)) & 7)) << 4));
           if (swap) o = make_uint4(o.z, o.w, o.x, o.y);
-          uint8_t* d = dst + k * stride;
-          const int valid = min(16, g.rows - p * 16);
-          if (valid == 16 && (reinterpret_cast<uintptr_t>(d) & 15) == 0) {
-            st_stream_v4(d, o);
-          } else {
-            const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
-            for (int b = 0; b < valid; ++b) d[b] = (uint8_t)(ow[b >> 2] >> (8 * (b & 3)));
-          }
+          const int src = (t & ~7) | ((p + 7) & 7);  // chunk (p-1) mod 8 of the same row
+          const uint4 prev = make_uint4(__shfl_sync(0xffffffffu, o.x, src & 31),
+                                        __shfl_sync(0xffffffffu, o.y, src & 31),
+                                        __shfl_sync(0xffffffffu, o.z, src & 31),
+                                        __shfl_sync(0xffffffffu, o.w, src & 31));
+          if (n < g.cols)
+            store_row_chunk(dst - p * 16 + k * stride, p, o, prev, g.rows, g.merge_in, g.carry_out,
+                            carry + n);
         }
       }
     }
@@ -582,7 +799,7 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
 }
 
 constexpr size_t kColTSmem = 128 + kColTStages * kColTCodeBytes + 128 * 128 + 8 * 128 * 4 +
-                             128 * 4 + 128 + 2 * 512 * 4 + 2 * 8 + 16;
+                             128 * 4 + 128 + 2 * 512 * 4 + 2 * 8 + 16 + 16 + 128 * 16;
 
 bool colT_attr() {
   static const bool ok =
@@ -673,7 +890,8 @@ extern "C" mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit(
   if (!make_tensor_map_2d(&tmap, input, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, total_M, N / 2, N / 2,
                           64, 128))
     return MXB_ERR_CUDA;
-  const int nb = (int)cdiv(max_split_len, 128);
+  // units of up to kUnitTiles row blocks along each segment
+  const int nb = (int)cdiv(cdiv(max_split_len, 128), kUnitTiles);
   const int64_t zt = cdiv(N, 128), tiles = zt * num_splits * nb;
   const int ctas = persistent_ctas((const void*)fp8_colT_kernel<true>, kThreads, kColTSmem);
   fp8_colT_kernel<true><<<(unsigned)min((int64_t)ctas, tiles), kThreads, kColTSmem,

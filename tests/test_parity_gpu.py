@@ -285,11 +285,13 @@ def test_mxfp4_to_fp8_colT(cuda, orc, shape, lo, hi):
     H.assert_bytes_equal(H.np_u8(q), rq, "fp8")
 
 
-@pytest.mark.parametrize("splits", [[128], [5, 128, 200, 0, 77], [1, 1, 1], [300, 129]])
+@pytest.mark.parametrize("splits,code_bytes", [([128], 80), ([5, 128, 200, 0, 77], 80),
+                                               ([1, 1, 1], 80), ([300, 129], 80),
+                                               ([1000, 3, 517, 256, 130], 256)])
 @pytest.mark.parametrize("lo,hi", [(117, 137), (0, 255)])
-def test_mxfp4_to_fp8_colT_split(cuda, orc, splits, lo, hi):
+def test_mxfp4_to_fp8_colT_split(cuda, orc, splits, code_bytes, lo, hi):
     M = sum(splits)
-    c, s = syn.config3(M, 80, seed=13, lo=lo, hi=hi)
+    c, s = syn.config3(M, code_bytes, seed=13, lo=lo, hi=hi)
     q, so = H.to_fp8_colT_split(c.to(cuda), s.to(cuda), splits)
     rq, rso = orc.mxfp4_to_fp8_colT_split(c.numpy(), s.numpy(), splits)
     H.assert_bytes_equal(H.np_f32(so).view(np.uint32), rso.view(np.uint32), "scales")
