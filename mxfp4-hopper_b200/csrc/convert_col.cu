@@ -546,12 +546,13 @@ __device__ __forceinline__ void store_row_chunk(uint8_t* row, int p, uint4 d, ui
       store_bytes16(base, v, lo, hi);
     }
   }
-  // memory chunk 8, bytes [0, a) (data 128 - a .. 127), if the block is full
-  if (a != 0 && len == 128) {
-    if (carry_out) {
+  // memory chunk 8: bytes [0, min(a, len + a - 128)) (data 128 - a .. len - 1),
+  // present when the segment reaches past memory chunk 7
+  if (a != 0 && len + a > 128) {
+    if (carry_out) {  // implies len == 128
       *carry = o;
     } else {
-      store_bytes16(base + 128, o, 0, a);
+      store_bytes16(base + 128, o, 0, min(a, len + a - 128));
     }
   }
 }
@@ -901,3 +902,4 @@ extern "C" mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit(
                                              (int)num_splits, nb, zt);
   return launch_status("mxfp4_to_fp8_colT_msplit");
 }
+

@@ -287,7 +287,8 @@ def test_mxfp4_to_fp8_colT(cuda, orc, shape, lo, hi):
 
 @pytest.mark.parametrize("splits,code_bytes", [([128], 80), ([5, 128, 200, 0, 77], 80),
                                                ([1, 1, 1], 80), ([300, 129], 80),
-                                               ([1000, 3, 517, 256, 130], 256)])
+                                               ([1000, 3, 517, 256, 130], 256),
+                                               ([250, 127, 383, 120, 1], 96)])
 @pytest.mark.parametrize("lo,hi", [(117, 137), (0, 255)])
 def test_mxfp4_to_fp8_colT_split(cuda, orc, splits, code_bytes, lo, hi):
     M = sum(splits)
