@@ -147,6 +147,24 @@ mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit(
     const int32_t* scale_offsets, int64_t num_splits, int64_t max_split_len, float eps,
     mxb_stream_t stream);
 
+/* No reference counterpart.  The same conversion with only m_splits (int32
+ * DEVICE [num_splits], e.g. straight from a router) and no caller-allocated
+ * offsets: split_offsets and scale_offsets are computed on the device, by a
+ * one-block exclusive scan on `stream`, into a file-scope device array of
+ * 2 x MXB_MSPLIT_MAX_SEGMENTS int32 (32 KiB per device); the call allocates
+ * nothing.  num_splits above MXB_MSPLIT_MAX_SEGMENTS is rejected with
+ * MXB_ERR_INVALID_ARGUMENT.  max_split_len must be at least every m_splits[i]
+ * (total_M always is); segments must sum to total_M.  Nothing in the array has
+ * to start at zero: the scan writes every word the conversion reads.  Calls
+ * that overlap on the GPU (on other streams, or from other host threads
+ * without ordering) share that array and race; order them, e.g. on one
+ * stream. */
+#define MXB_MSPLIT_MAX_SEGMENTS 4096
+mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit_noalloc(
+    const void* input, const void* input_s, int64_t total_M, int64_t N, void* output_q,
+    void* output_s, const int32_t* m_splits, int64_t num_splits, int64_t max_split_len, float eps,
+    mxb_stream_t stream);
+
 /* ------------------------------------------------------------ per-token FP8 */
 
 /* BF16 -> FP8 E4M3 with one FP32 scale per row: amax = max(eps, max|x|),

@@ -16,6 +16,7 @@
 // are transposed through shared memory and leave as 128-byte runs of output
 // rows, eight lanes per run.  Several CTAs per SM overlap one tile's load
 // with the others' work.
+#include <mutex>
 #include <type_traits>
 
 #include "capi_util.h"
@@ -813,6 +814,69 @@ bool colT_attr() {
   return ok;
 }
 
+// ------------------------------------------------ msplit without allocation
+// Scratch of the allocation-free split entry point: split_offsets in words
+// [0, kMaxSeg), scale_offsets in [kMaxSeg, 2 kMaxSeg).  32 KiB per device.
+constexpr int kMaxSeg = MXB_MSPLIT_MAX_SEGMENTS;
+static __device__ __align__(256) int32_t g_msplit_scratch[2 * kMaxSeg];
+
+// One block of 1024 threads: exclusive scans of m_i (row offsets) and of
+// ceil(m_i / 128) (scale-row offsets); thread t owns segments 4t .. 4t+3.
+__global__ void __launch_bounds__(1024) msplit_offsets_kernel(const int32_t* __restrict__ m_splits,
+                                                             int ns, int32_t* __restrict__ so,
+                                                             int32_t* __restrict__ sco) {
+  __shared__ int32_t warp_rows[32], warp_blocks[32];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  int32_t m[4], rows = 0, blocks = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = 4 * t + j;
+    m[j] = i < ns ? m_splits[i] : 0;
+    rows += m[j];
+    blocks += (m[j] + 127) / 128;
+  }
+  // inclusive warp scans, then the warp totals
+  int32_t ir = rows, ib = blocks;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t r = __shfl_up_sync(0xffffffffu, ir, o), b = __shfl_up_sync(0xffffffffu, ib, o);
+    if (lane >= o) {
+      ir += r;
+      ib += b;
+    }
+  }
+  if (lane == 31) {
+    warp_rows[warp] = ir;
+    warp_blocks[warp] = ib;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int32_t wr = warp_rows[lane], wb = warp_blocks[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t r = __shfl_up_sync(0xffffffffu, wr, o), b = __shfl_up_sync(0xffffffffu, wb, o);
+      if (lane >= o) {
+        wr += r;
+        wb += b;
+      }
+    }
+    warp_rows[lane] = wr - warp_rows[lane];  // exclusive prefix of the warp totals
+    warp_blocks[lane] = wb - warp_blocks[lane];
+  }
+  __syncthreads();
+  int32_t r0 = warp_rows[warp] + ir - rows, b0 = warp_blocks[warp] + ib - blocks;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = 4 * t + j;
+    if (i < ns) {
+      so[i] = r0;
+      sco[i] = b0;
+    }
+    r0 += m[j];
+    b0 += (m[j] + 127) / 128;
+  }
+}
+
 }  // namespace
 }  // namespace mxb
 
@@ -903,3 +967,43 @@ extern "C" mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit(
   return launch_status("mxfp4_to_fp8_colT_msplit");
 }
 
+// Device address of g_msplit_scratch, looked up once per device with that
+// device current (a module's __device__ arrays exist once per device).
+static int32_t* msplit_scratch() {
+  static std::mutex mu;
+  static int32_t* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_msplit_scratch) != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<int32_t*>(p);
+  }
+  return addr[dev];
+}
+
+extern "C" mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit_noalloc(
+    const void* input, const void* input_s, int64_t total_M, int64_t N, void* output_q,
+    void* output_s, const int32_t* m_splits, int64_t num_splits, int64_t max_split_len, float eps,
+    mxb_stream_t stream) {
+  MXB_REQUIRE(num_splits >= 0 && num_splits <= kMaxSeg, MXB_ERR_INVALID_ARGUMENT,
+              "mxfp4_to_fp8_colT_msplit_noalloc: num_splits = %lld exceeds the %d segments of "
+              "the static scratch (use mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit)",
+              (long long)num_splits, kMaxSeg);
+  MXB_REQUIRE(total_M >= 0 && total_M <= INT32_MAX && max_split_len >= 0, MXB_ERR_INVALID_ARGUMENT,
+              "mxfp4_to_fp8_colT_msplit_noalloc: need 0 <= total_M <= 2^31-1 and max_split_len >= 0");
+  if (total_M == 0 || N == 0 || num_splits == 0 || max_split_len == 0) return MXB_OK;
+  MXB_REQUIRE(m_splits, MXB_ERR_INVALID_ARGUMENT, "mxfp4_to_fp8_colT_msplit_noalloc: null m_splits");
+  int32_t* scratch = msplit_scratch();
+  MXB_REQUIRE(scratch, MXB_ERR_CUDA,
+              "mxfp4_to_fp8_colT_msplit_noalloc: cannot look up the static scratch (%s)",
+              cudaGetErrorString(cudaGetLastError()));
+  msplit_offsets_kernel<<<1, 1024, 0, to_cuda(stream)>>>(m_splits, (int)num_splits, scratch,
+                                                         scratch + kMaxSeg);
+  const mxb_status st = launch_status("mxfp4_to_fp8_colT_msplit_noalloc (offsets)");
+  if (st != MXB_OK) return st;
+  return mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit(input, input_s, total_M, N, output_q, output_s,
+                                                     m_splits, scratch, scratch + kMaxSeg,
+                                                     num_splits, max_split_len, eps, stream);
+}

@@ -30,6 +30,8 @@ SIGNATURES = {
     "mxb_per_token_Mxfp4RowToBf16ToFp8Col": [_P, _P, _I64, _I64, _P, _P, _F, _P],
     "mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit": [_P, _P, _I64, _I64, _P, _P, _P, _P, _P,
                                                     _I64, _I64, _F, _P],
+    "mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit_noalloc": [_P, _P, _I64, _I64, _P, _P, _P, _I64,
+                                                            _I64, _F, _P],
     "mxb_per_token_quant_fp8": [_P, _I64, _I64, _P, _P, _F, _P],
     "mxb_per_token_dequant_fp8": [_P, _P, _I64, _I64, _P, _P],
     "mxb_ep_pack": [_P, _I64, _I64, _P, _I, _P, _F, _P],
