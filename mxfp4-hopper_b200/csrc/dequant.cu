@@ -72,7 +72,8 @@ __global__ void __launch_bounds__(256) dq_bf16_kernel(const uint8_t* __restrict_
 // A lane converts 8 code bytes (16 elements, half a 32-element block) into one
 // 16-byte FP8 store; eight lanes cover one 1x128 group and read the group's
 // four E8M0 bytes as one word.  The element arithmetic is a lookup in the
-// compile-time table row for d = max_e - e (fp8_lut.cuh).
+// compile-time table row for d = max_e - e (fp8_lut.cuh).  Four chunks per lane
+// are in flight per iteration.
 __device__ const Fp8Lut g_lut_row = make_fp8_lut(false);
 
 __device__ __forceinline__ uint32_t max_u8x4(uint32_t s) {
@@ -81,6 +82,8 @@ __device__ __forceinline__ uint32_t max_u8x4(uint32_t s) {
   return max(a, b);
 }
 
+constexpr int kFp8RowUnroll = 4;
+
 __global__ void __launch_bounds__(256) dq_fp8_row_kernel(const uint8_t* __restrict__ codes,
                                                          const uint8_t* __restrict__ scales,
                                                          int64_t M, int64_t Kb,
@@ -88,35 +91,53 @@ __global__ void __launch_bounds__(256) dq_fp8_row_kernel(const uint8_t* __restri
                                                          float* __restrict__ scales_out) {
   const int64_t lanes_total = M * Kb / 8;  // one lane per 8 code bytes
   const int64_t groups_per_row = Kb / 64;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 2;
-  for (int64_t base = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) * 2;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * kFp8RowUnroll;
+  const int lane = threadIdx.x & 31;
+  for (int64_t base = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) * kFp8RowUnroll;
        base < lanes_total; base += stride) {
-    uint2 w[2];
-    uint32_t sw[2];
+    // all loads of the iteration first (codes, then the groups' scale words,
+    // then the table rows they select), then the arithmetic and the stores
+    uint2 w[kFp8RowUnroll];
+    uint32_t sw[kFp8RowUnroll];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int64_t l = base + k * 32 + (threadIdx.x & 31);
+    for (int k = 0; k < kFp8RowUnroll; ++k) {
+      const int64_t l = base + k * 32 + lane;
       if (l < lanes_total) {
         w[k] = ld_stream_v2(codes + l * 8);
         sw[k] = ld_stream_u32(scales + (l >> 3) * 4);
+      } else {
+        w[k] = make_uint2(0u, 0u);
+        sw[k] = 0u;
       }
     }
+    uint32_t mx[kFp8RowUnroll];
+    uint4 t[kFp8RowUnroll];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int64_t l = base + k * 32 + (threadIdx.x & 31);
-      if (l >= lanes_total) continue;
-      const uint32_t mx = max_u8x4(sw[k]);
+    for (int k = 0; k < kFp8RowUnroll; ++k) {
+      const int64_t l = base + k * 32 + lane;
+      mx[k] = max_u8x4(sw[k]);
       const uint32_t e = (sw[k] >> (8 * ((l >> 1) & 3))) & 0xFFu;
-      const uint4 t = __ldg(reinterpret_cast<const uint4*>(g_lut_row.v[mx - e]));
-      const uint4 o = make_uint4(lut_lookup4(w[k].x, t.x, t.y, t.z, t.w),
-                                 lut_lookup4(w[k].x >> 16, t.x, t.y, t.z, t.w),
-                                 lut_lookup4(w[k].y, t.x, t.y, t.z, t.w),
-                                 lut_lookup4(w[k].y >> 16, t.x, t.y, t.z, t.w));
+      t[k] = __ldg(reinterpret_cast<const uint4*>(g_lut_row.v[mx[k] - e]));
+    }
+#pragma unroll
+    for (int k = 0; k < kFp8RowUnroll; ++k) {
+      const int64_t l = base + k * 32 + lane;
+      if (l >= lanes_total) continue;
+      const uint4 o = make_uint4(lut_lookup4(w[k].x, t[k].x, t[k].y, t[k].z, t[k].w),
+                                 lut_lookup4(w[k].x >> 16, t[k].x, t[k].y, t[k].z, t[k].w),
+                                 lut_lookup4(w[k].y, t[k].x, t[k].y, t[k].z, t[k].w),
+                                 lut_lookup4(w[k].y >> 16, t[k].x, t[k].y, t[k].z, t[k].w));
       st_stream_v4(out + l * 16, o);
       if ((l & 7) == 0) {
         const int64_t grp = l >> 3;
-        const int64_t r = grp / groups_per_row, gc = grp - r * groups_per_row;
-        scales_out[gc * M + r] = __uint_as_float(((mx - 6u) & 0xFFu) << 23);
+        int64_t r;
+        if (grp <= (int64_t)UINT32_MAX) {  // 32-bit division whenever it suffices
+          r = (uint32_t)grp / (uint32_t)groups_per_row;
+        } else {
+          r = grp / groups_per_row;
+        }
+        const int64_t gc = grp - r * groups_per_row;
+        scales_out[gc * M + r] = __uint_as_float(((mx[k] - 6u) & 0xFFu) << 23);
       }
     }
   }
@@ -162,7 +183,7 @@ extern "C" mxb_status mxb_per_token_Mxfp4ToFp8(const void* input, const void* in
                   aligned(output_s, 4),
               MXB_ERR_MISALIGNED, "mxfp4_to_fp8: misaligned pointer");
   const int64_t lanes = M * Kb / 8;
-  const int grid = grid_for((const void*)dq_fp8_row_kernel, lanes, 2);
+  const int grid = grid_for((const void*)dq_fp8_row_kernel, lanes, kFp8RowUnroll);
   dq_fp8_row_kernel<<<grid, 256, 0, to_cuda(stream)>>>((const uint8_t*)input,
                                                        (const uint8_t*)input_s, M, Kb,
                                                        (uint8_t*)output_q, (float*)output_s);
