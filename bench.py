@@ -407,7 +407,15 @@ def time_other_ops(dev, stream, peak):
         lambda: capi.call("mxb_per_token_group_quant_fp4", x.data_ptr(), M2, K2, K2, q.data_ptr(),
                           s.data_ptr(), 32, 1e-10, -6.0, 6.0, 0, sh),
         M2 * K2 * 2 + M2 * K2 // 2 + M2 * K2 // 32)
-    del x, q, s
+    # Q-row fused with its rowwise FP8 conversion (omo_per_token_group_quant_fp4_fused_ToFp8)
+    f8q = torch.empty(M2, K2, dtype=torch.uint8, device=dev)
+    f8s = torch.empty(K2 // 128, M2, dtype=torch.float32, device=dev)
+    res["quant_fused_fp8_config2"] = timeit(
+        lambda: capi.call("mxb_per_token_group_quant_fp4_fused_ToFp8", x.data_ptr(), M2, K2, K2,
+                          q.data_ptr(), s.data_ptr(), f8q.data_ptr(), f8s.data_ptr(), 32, 1e-10,
+                          -6.0, 6.0, 0, sh),
+        M2 * K2 * 2 + M2 * K2 // 2 + M2 * K2 // 32 + M2 * K2 + f8s.numel() * 4)
+    del x, q, s, f8q, f8s
     # config 3: codes [16384, 8192] u8 (K = 16384 elements), scales [16384, 512]
     c, sc = (t.to(dev) for t in syn.config3())
     M3, Kb3 = c.shape

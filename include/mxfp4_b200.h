@@ -65,6 +65,19 @@ mxb_status mxb_per_token_group_quant_fp4(const void* input, int64_t M, int64_t K
                                          float eps, float fp4_min, float fp4_max,
                                          int scale_ue8m0, mxb_stream_t stream);
 
+/* Q-row and the rowwise FP8 convert of its result in one pass: output_q /
+ * output_s exactly as mxb_per_token_group_quant_fp4, output_fp8 [M, K] E4M3 and
+ * output_fp8_s float [K/128, M] exactly as mxb_per_token_Mxfp4ToFp8 applied to
+ * them, without re-reading the codes.  K % 128 == 0.  Replaces
+ * omo_per_token_group_quant_fp4_fused_ToFp8 (code/kernel/ops.cu:34-35, whose
+ * source the reference does not ship; this is its two shipped halves fused). */
+mxb_status mxb_per_token_group_quant_fp4_fused_ToFp8(const void* input, int64_t M, int64_t K,
+                                                     int64_t ldx, void* output_q, void* output_s,
+                                                     void* output_fp8, void* output_fp8_s,
+                                                     int group_size, float eps, float fp4_min,
+                                                     float fp4_max, int scale_ue8m0,
+                                                     mxb_stream_t stream);
+
 /* Rowwise AND columnwise BF16 -> MXFP4 in one pass over the input.
  * Replaces the Transformer Engine quantize of the reference
  * (code/transformer_engine-2.8.diff:1464-1466): rowwise = Q-row of input,

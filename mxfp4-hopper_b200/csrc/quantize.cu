@@ -28,6 +28,7 @@
 
 #include "capi_util.h"
 #include "common.cuh"
+#include "fp8_lut.cuh"
 #include "tma.cuh"
 
 namespace mxb {
@@ -234,12 +235,25 @@ __device__ __forceinline__ int64_t swizzle_offset(int64_t r, int64_t c, int64_t 
 // ------------------------------------------------------------------ Q-row
 // Two lanes per 32-element block, 16 elements (two 16-byte loads) per lane.
 // A warp covers 16 consecutive blocks: 1 KiB of contiguous input per step.
-template <bool kFast>
+//
+// With kFp8 the same pass also writes the rowwise FP8 conversion of the codes
+// it has just produced (the reference op omo_per_token_group_quant_fp4_fused_ToFp8,
+// bound at code/kernel/ops.cu:34 with no source shipped), bit-identical to
+// running the rowwise FP8 converter (per_token_Mxfp4ToFp8.cu:157-233) on this
+// kernel's output: a lane's 8 code bytes are exactly one lane of that
+// converter, the 8 lanes of a 1x128 group are adjacent in the warp (K % 128 ==
+// 0), so the group max of the four E8M0 bytes is two shuffles, and each lane
+// maps its nibbles through the table row for d = max - e (fp8_lut.cuh).  The
+// codes are never re-read from HBM.
+__device__ const Fp8Lut g_lut_fused = make_fp8_lut(false);
+
+template <bool kFast, bool kFp8>
 __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __restrict__ x,
                                                          int64_t M, int64_t K, int64_t ldx,
                                                          uint8_t* __restrict__ codes,
                                                          uint8_t* __restrict__ scales,
-                                                         QuantParams p) {
+                                                         QuantParams p, uint8_t* __restrict__ fp8,
+                                                         float* __restrict__ fp8_s) {
   const int64_t G = K >> 5;
   const int64_t halves = M * G * 2;
   const int lane = threadIdx.x & 31;
@@ -276,6 +290,18 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __
     }
     st_stream_v2(codes + r * (K >> 1) + g * 16 + half * 8, make_uint2(out[0], out[1]));
     if (half == 0) scales[r * G + g] = (uint8_t)byte;
+    if (kFp8) {
+      const unsigned group_mask = 0xFFu << (lane & ~7);
+      uint32_t mx = max(byte, __shfl_xor_sync(group_mask, byte, 2));
+      mx = max(mx, __shfl_xor_sync(group_mask, mx, 4));
+      const uint4 t = __ldg(reinterpret_cast<const uint4*>(g_lut_fused.v[mx - byte]));
+      const uint4 o = make_uint4(lut_lookup4(out[0], t.x, t.y, t.z, t.w),
+                                 lut_lookup4(out[0] >> 16, t.x, t.y, t.z, t.w),
+                                 lut_lookup4(out[1], t.x, t.y, t.z, t.w),
+                                 lut_lookup4(out[1] >> 16, t.x, t.y, t.z, t.w));
+      st_stream_v4(fp8 + r * K + g * 32 + half * 16, o);
+      if ((h & 7) == 0) fp8_s[(g >> 2) * M + r] = __uint_as_float(((mx - 6u) & 0xFFu) << 23);
+    }
   }
 }
 
@@ -501,6 +527,27 @@ bool fast_params(float eps, float fp4_min, float fp4_max) {
   return fp4_max == 6.0f && fp4_min == -6.0f && eps >= 0.0f && eps <= 6e-10f;
 }
 
+template <bool kFp8>
+void launch_quant_rows(bool fast, const void* input, int64_t M, int64_t K, int64_t ldx,
+                       void* output_q, void* output_s, const QuantParams& p, void* fp8, void* fp8_s,
+                       mxb_stream_t stream) {
+  const void* kern = fast ? (const void*)quant_rows_kernel<true, kFp8>
+                          : (const void*)quant_rows_kernel<false, kFp8>;
+  const int64_t halves = M * (K / 32) * 2;
+  const int64_t want = cdiv(halves, 256);
+  const int64_t cap = (int64_t)persistent_ctas(kern, 256, 0) * 4;
+  const int grid = (int)(want < cap ? want : cap);
+  if (fast)
+    quant_rows_kernel<true, kFp8><<<grid, 256, 0, to_cuda(stream)>>>(
+        (const __nv_bfloat16*)input, M, K, ldx, (uint8_t*)output_q, (uint8_t*)output_s, p,
+        (uint8_t*)fp8, (float*)fp8_s);
+  else
+    quant_rows_kernel<false, kFp8><<<grid, 256, 0, to_cuda(stream)>>>(
+        (const __nv_bfloat16*)input, M, K, ldx, (uint8_t*)output_q, (uint8_t*)output_s, p,
+        (uint8_t*)fp8, (float*)fp8_s);
+}
+
+
 }  // namespace
 }  // namespace mxb
 
@@ -526,18 +573,35 @@ extern "C" mxb_status mxb_per_token_group_quant_fp4(const void* input, int64_t M
               "quant_fp4: input must be 16-byte and output_q 8-byte aligned");
   const QuantParams p{eps, fp4_min, fp4_max};
   const bool fast = fast_params(eps, fp4_min, fp4_max);
-  const void* kern = fast ? (const void*)quant_rows_kernel<true> : (const void*)quant_rows_kernel<false>;
-  const int64_t halves = M * (K / 32) * 2;
-  int64_t want = cdiv(halves, 256);
-  const int64_t cap = (int64_t)persistent_ctas(kern, 256, 0) * 4;
-  const int grid = (int)(want < cap ? want : cap);
-  if (fast)
-    quant_rows_kernel<true><<<grid, 256, 0, to_cuda(stream)>>>(
-        (const __nv_bfloat16*)input, M, K, ldx, (uint8_t*)output_q, (uint8_t*)output_s, p);
-  else
-    quant_rows_kernel<false><<<grid, 256, 0, to_cuda(stream)>>>(
-        (const __nv_bfloat16*)input, M, K, ldx, (uint8_t*)output_q, (uint8_t*)output_s, p);
+  launch_quant_rows<false>(fast, input, M, K, ldx, output_q, output_s, p, nullptr, nullptr, stream);
   return launch_status("quant_fp4");
+}
+
+extern "C" mxb_status mxb_per_token_group_quant_fp4_fused_ToFp8(
+    const void* input, int64_t M, int64_t K, int64_t ldx, void* output_q, void* output_s,
+    void* output_fp8, void* output_fp8_s, int group_size, float eps, float fp4_min, float fp4_max,
+    int scale_ue8m0, mxb_stream_t stream) {
+  MXB_REQUIRE(group_size == 32, MXB_ERR_UNSUPPORTED,
+              "quant_fp4_fused_fp8: group_size must be 32 (got %d)", group_size);
+  MXB_REQUIRE(!scale_ue8m0, MXB_ERR_UNSUPPORTED,
+              "quant_fp4_fused_fp8: scale_ue8m0=True is rejected, as by the reference host assert");
+  MXB_REQUIRE(M >= 0 && K >= 0 && K % 128 == 0, MXB_ERR_INVALID_ARGUMENT,
+              "quant_fp4_fused_fp8: need K %% 128 == 0 (1x128 FP8 groups), got M=%lld K=%lld",
+              (long long)M, (long long)K);
+  MXB_REQUIRE(ldx >= K && ldx % 8 == 0, MXB_ERR_MISALIGNED,
+              "quant_fp4_fused_fp8: row pitch must be >= K and a multiple of 8 elements");
+  if (M == 0 || K == 0) return MXB_OK;
+  MXB_REQUIRE(input && output_q && output_s && output_fp8 && output_fp8_s, MXB_ERR_INVALID_ARGUMENT,
+              "quant_fp4_fused_fp8: null pointer");
+  MXB_REQUIRE(aligned(input, 16) && aligned(output_q, 8) && aligned(output_fp8, 16) &&
+                  aligned(output_fp8_s, 4),
+              MXB_ERR_MISALIGNED,
+              "quant_fp4_fused_fp8: input and output_fp8 must be 16-byte, output_q 8-byte and "
+              "output_fp8_s 4-byte aligned");
+  const QuantParams p{eps, fp4_min, fp4_max};
+  launch_quant_rows<true>(fast_params(eps, fp4_min, fp4_max), input, M, K, ldx, output_q, output_s,
+                          p, output_fp8, output_fp8_s, stream);
+  return launch_status("quant_fp4_fused_fp8");
 }
 
 extern "C" mxb_status mxb_quant_mxfp4_rowcol(const void* input, int64_t M, int64_t K, int64_t ldx,

@@ -22,6 +22,8 @@ _F = ctypes.c_float
 SIGNATURES = {
     "mxb_per_token_group_quant_fp4": [_P, _I64, _I64, _I64, _P, _P, _I, _F, _F, _F, _I, _P],
     "mxb_quant_mxfp4_rowcol": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _F, _F, _F, _P],
+    "mxb_per_token_group_quant_fp4_fused_ToFp8": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _I, _F,
+                                                  _F, _F, _I, _P],
     "mxb_swizzle_scales": [_P, _I64, _I64, _P, _P],
     "mxb_per_token_Mxfp4ToBf16_dequant": [_P, _P, _I64, _I64, _P, _P],
     "mxb_per_token_Mxfp4ToFp8": [_P, _P, _I64, _I64, _P, _P, _P],

@@ -9,7 +9,8 @@ from typing import Optional
 import torch
 
 import mxfp4_b200  # noqa: F401
-from omo import omo_per_token_group_quant_fp4, omo_quant_mxfp4_rowcol
+from omo import (omo_per_token_group_quant_fp4, omo_per_token_group_quant_fp4_fused_ToFp8,
+                 omo_quant_mxfp4_rowcol)
 
 fp8_type_ = torch.float8_e4m3fn
 uint8_type = torch.uint8
@@ -121,3 +122,21 @@ def omo_per_token_group_quant_mxfp4_rowcol(x: torch.Tensor, rowwise: bool = True
     omo_quant_mxfp4_rowcol(x, cr, sr, cc, sc, swz)
     out = (cr if rowwise else None, sr if rowwise else None, cc, sc)
     return out + (swz,) if swizzled_scales else out
+
+
+def omo_per_token_group_quant_mxfp4_fused_fp8(x: torch.Tensor):
+    """Rowwise MXFP4 quantize and its rowwise FP8 conversion in one pass (the op
+    the reference binds as omo_per_token_group_quant_fp4_fused_ToFp8, ops.cu:34,
+    without a shipped wrapper).  Returns (codes [M, K/2] uint8, E8M0 scales
+    [M, K/32] uint8, FP8 [M, K], FP32 group scales [K/128, M]); K % 128 == 0."""
+    assert x.dim() == 2 and x.is_contiguous(), "`x` must be a contiguous 2-D tensor"
+    M, K = x.shape
+    dev = x.device
+    x_q = torch.empty((M, K // 2), device=dev, dtype=uint8_type)
+    x_s = torch.empty((M, K // 32), device=dev, dtype=uint8_type)
+    y = torch.empty((M, K), device=dev, dtype=fp8_type_)
+    y_s = torch.empty((K // 128, M), device=dev, dtype=torch.float)
+    if M > 0:
+        omo_per_token_group_quant_fp4_fused_ToFp8(x, x_q, x_s, y, y_s, 32, 1e-10, mxfp4_min,
+                                                  mxfp4_max, False)
+    return x_q, x_s, y, y_s

@@ -47,7 +47,12 @@ void omo_per_token_group_quant_fp4(at::Tensor input, at::Tensor output_q, at::Te
   if (input.numel() == 0) return;
   const int64_t K = input.size(-1), M = input.numel() / K;
   TORCH_CHECK(output_q.numel() == M * K / 2, "output_q must hold numel/2 bytes");
-  TORCH_CHECK(output_s.numel() == M * K / 32, "output_s must hold numel/32 scales");
+  // The reference writes group g's scale at output_s.data_ptr() + g whatever the
+  // tensor's shape (per_token_quant_mxfp4.cu:161), and its fp4 wrapper sizes
+  // output_s from the code shape, [M, K/2] (api/mxfp4.py:106-111): any
+  // contiguous buffer of at least numel/32 bytes is accepted and the scales
+  // fill its first numel/32 bytes.
+  TORCH_CHECK(output_s.numel() >= M * K / 32, "output_s must hold numel/32 scales");
   c10::cuda::CUDAGuard g(input.device());
   check_status(mxb_per_token_group_quant_fp4(input.data_ptr(), M, K, K, output_q.data_ptr(),
                                              output_s.data_ptr(), (int)group_size, (float)eps,
@@ -137,13 +142,34 @@ void omo_per_token_group_quant_fp4_fused_ToFp8(at::Tensor input, at::Tensor outp
                                                at::Tensor output_bf16_s, int64_t group_size,
                                                double eps, double fp4_min, double fp4_max,
                                                bool scale_ue8m0) {
-  omo_per_token_group_quant_fp4(input, output_q, output_s, group_size, eps, fp4_min, fp4_max,
-                                scale_ue8m0);
+  // the checks of both halves (omo_per_token_group_quant_fp4 and omo_per_token_Mxfp4ToFp8)
+  OMO_CHECK_INPUT(input);
+  OMO_CHECK_INPUT(output_q);
+  OMO_CHECK_INPUT(output_bf16_q);
+  TORCH_CHECK(input.numel() % group_size == 0, "CHECK_EQ(input.numel() % group_size, 0) failed");
+  TORCH_CHECK(output_s.dim() == 2 && output_bf16_s.dim() == 2, "CHECK_EQ(output_s.dim(), 2) failed");
+  check_dtype(input, at::kBFloat16, "input");
+  check_dtype(output_q, at::kByte, "output_q");
+  check_dtype(output_s, at::kByte, "output_s");
+  check_dtype(output_bf16_q, at::kFloat8_e4m3fn, "output_bf16_q");
+  check_dtype(output_bf16_s, at::kFloat, "output_bf16_s");
+  TORCH_CHECK(output_s.is_contiguous() && output_s.is_cuda() && output_bf16_s.is_contiguous() &&
+                  output_bf16_s.is_cuda(),
+              "scale outputs must be contiguous CUDA tensors");
   if (input.numel() == 0) return;
   const int64_t K = input.size(-1), M = input.numel() / K;
-  at::Tensor q2 = output_q.view({M, K / 2});
-  mxfp4_to_fp8_row_common(q2, output_s, output_bf16_q, output_bf16_s, false,
-                          "omo_per_token_group_quant_fp4_fused_ToFp8");
+  TORCH_CHECK(K % 128 == 0, "omo_per_token_group_quant_fp4_fused_ToFp8: K must be a multiple of "
+              "128 (1x128 FP8 groups)");
+  TORCH_CHECK(output_q.numel() == M * K / 2, "output_q must hold numel/2 bytes");
+  TORCH_CHECK(output_s.numel() >= M * K / 32, "output_s must hold numel/32 scales");
+  TORCH_CHECK(output_bf16_q.numel() == M * K, "output_bf16_q must be [M, K]");
+  TORCH_CHECK(output_bf16_s.numel() == M * K / 128, "output_bf16_s must be [K/128, M]");
+  c10::cuda::CUDAGuard g(input.device());
+  check_status(mxb_per_token_group_quant_fp4_fused_ToFp8(
+                   input.data_ptr(), M, K, K, output_q.data_ptr(), output_s.data_ptr(),
+                   output_bf16_q.data_ptr(), output_bf16_s.data_ptr(), (int)group_size, (float)eps,
+                   (float)fp4_min, (float)fp4_max, scale_ue8m0 ? 1 : 0, cur_stream()),
+               "omo_per_token_group_quant_fp4_fused_ToFp8");
 }
 
 // ---- per_token_Mxfp4ToFp8_col.cu:305-384

@@ -42,6 +42,18 @@ def quant_rows(x, eps=1e-10, fmin=-6.0, fmax=6.0):
     return q, s
 
 
+def quant_fused_fp8(x, eps=1e-10, fmin=-6.0, fmax=6.0):
+    """Q-row and its rowwise FP8 conversion in one launch."""
+    M, K = x.shape
+    q = torch.empty(M, K // 2, dtype=torch.uint8, device=x.device)
+    s = torch.empty(M, K // 32, dtype=torch.uint8, device=x.device)
+    f = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=x.device)
+    fs = torch.empty(K // 128, M, dtype=torch.float32, device=x.device)
+    capi.call("mxb_per_token_group_quant_fp4_fused_ToFp8", dp(x), M, K, K, dp(q), dp(s), dp(f),
+              dp(fs), 32, eps, fmin, fmax, 0, stream())
+    return q, s, f, fs
+
+
 def quant_rowcol(x, rows=True, swz=False, eps=1e-10, fmin=-6.0, fmax=6.0):
     M, K = x.shape
     dev = x.device

@@ -115,6 +115,45 @@ def test_quant_rows_generic_params(cuda, orc, eps, fmin, fmax):
     H.assert_bytes_equal(H.np_u8(q), rq, "codes")
 
 
+# -------------------------------------------- fused Q-row + rowwise FP8
+def _fused_cases():
+    x = syn.config1(64, 1024, seed=8)
+    sp = special_block_input()
+    sp128 = np.concatenate([sp, sp[:, ::-1]], axis=1)  # 128 columns: 1x128 FP8 groups
+    return {
+        "config1": (_bits(x), (1e-10, -6.0, 6.0)),
+        "special": (sp128, (1e-10, -6.0, 6.0)),
+        "generic": (np.concatenate([_bits(x), sp128.repeat(8, 1)]), (1e-3, -4.0, 4.0)),
+        "deep_exponents": (_bits(syn.config2(32, 7168, seed=9)), (1e-10, -6.0, 6.0)),
+    }
+
+
+@pytest.mark.parametrize("case", ["config1", "special", "generic", "deep_exponents"])
+def test_quant_fused_fp8(cuda, orc, case):
+    """One pass equals Q-row followed by the rowwise FP8 convert, byte for byte,
+    against the oracle and against the two separate launches."""
+    xb, (eps, fmin, fmax) = _fused_cases()[case]
+    q, s, f, fs = H.quant_fused_fp8(to_dev_bf16(xb, cuda), eps, fmin, fmax)
+    rq, rs = orc.quant_rows(xb, eps, fmin, fmax)
+    H.assert_bytes_equal(H.np_u8(s), rs, "scales")
+    H.assert_bytes_equal(H.np_u8(q), rq, "codes")
+    rf, rfs = orc.mxfp4_to_fp8_rows(rq, rs)
+    H.assert_bytes_equal(H.np_u8(f), rf, "fp8")
+    H.assert_bytes_equal(H.np_f32(fs).view(np.uint32), rfs.view(np.uint32), "fp8 scales")
+    q2, s2 = H.quant_rows(to_dev_bf16(xb, cuda), eps, fmin, fmax)
+    f2, fs2 = H.to_fp8_rows(q2, s2)
+    H.assert_bytes_equal(H.np_u8(f), H.np_u8(f2), "fp8 vs two launches")
+
+
+def test_quant_fused_fp8_rejects_k_not_128(cuda):
+    from mxfp4_b200 import capi
+    x = torch.zeros(4, 96, dtype=torch.bfloat16, device=cuda)
+    st = capi.status_of("mxb_per_token_group_quant_fp4_fused_ToFp8", x.data_ptr(), 4, 96, 96,
+                        x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(), 32, 1e-10, -6.0,
+                        6.0, 0, H.stream())
+    assert st == 1 and "128" in capi.last_error()
+
+
 def test_quant_rows_strided_input(cuda, orc):
     from mxfp4_b200 import capi
     x = syn.config2(64, 512, seed=5)
