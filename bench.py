@@ -172,6 +172,9 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ops", action="store_true")
+    ap.add_argument("--profile-op", default=None,
+                    help="run only this entry of `ops` (3 + 3 launches on its BASELINE shape, "
+                         "no JSON line): the command the ncu summaries in profiles/ were made with")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -190,6 +193,12 @@ def main():
     capi.load()
     peak, peak_kind = measured_peaks()
     warm = max(args.warmup, 3)
+    if args.profile_op:
+        res = time_other_ops(dev, torch.cuda.current_stream(dev), peak, only=args.profile_op)
+        if not res:
+            raise SystemExit(f"unknown --profile-op {args.profile_op}")
+        print(json.dumps(res), file=sys.stderr)
+        return 0
 
     x = syn.config2().to(dev)
     cr = torch.empty(M2, K2 // 2, dtype=torch.uint8, device=dev)
@@ -376,8 +385,9 @@ def time_ep(dev, stream, world, rank, args):
                                 "frac": round(floor_ms / ms2, 4)}}
 
 
-def time_other_ops(dev, stream, peak):
-    """Device-resident GB/s of the other kernels of the path on their BASELINE shapes."""
+def time_other_ops(dev, stream, peak, only=None):
+    """Device-resident GB/s of the other kernels of the path on their BASELINE shapes
+    (with `only`, just that entry, 3 + 3 launches)."""
     import torch
 
     from mxfp4_b200 import capi
@@ -386,7 +396,14 @@ def time_other_ops(dev, stream, peak):
     sh = stream.cuda_stream
     res = {}
 
-    def timeit(fn, alg_bytes, n=20):
+    def want(*names):
+        return only is None or only in names
+
+    def timeit(name, fn, alg_bytes, n=20):
+        if not want(name):
+            return
+        if only is not None:
+            n = 3
         for _ in range(3):
             fn()
         torch.cuda.synchronize(dev)
@@ -398,46 +415,62 @@ def time_other_ops(dev, stream, peak):
         torch.cuda.synchronize(dev)
         ms = a.elapsed_time(b) / n
         gbs = alg_bytes / (ms * 1e-3) / 1e9
-        return {"us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+        res[name] = {"us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
 
+    C3 = ("dequant_bf16_config3", "mxfp4_to_fp8_rows_config3", "mxfp4_to_fp8_col_config3",
+          "mxfp4_to_fp8_colT_config3", "mxfp4_to_fp8_colT_msplit8_config3")
     # Q-row alone on config 2
+    if want("quant_rows_config2", "quant_fused_fp8_config2"):
+        _ops_config2(dev, sh, timeit, capi, syn)
+    if want(*C3):
+        _ops_config3(dev, sh, timeit, capi, syn)
+    if want("fp8_quant_config4", "fp8_dequant_config4"):
+        _ops_config4(dev, sh, timeit, capi, syn)
+    return res
+
+
+def _ops_config2(dev, sh, timeit, capi, syn):
+    import torch
     x = syn.config2().to(dev)
     q = torch.empty(M2, K2 // 2, dtype=torch.uint8, device=dev)
     s = torch.empty(M2, K2 // 32, dtype=torch.uint8, device=dev)
-    res["quant_rows_config2"] = timeit(
+    timeit("quant_rows_config2",
         lambda: capi.call("mxb_per_token_group_quant_fp4", x.data_ptr(), M2, K2, K2, q.data_ptr(),
                           s.data_ptr(), 32, 1e-10, -6.0, 6.0, 0, sh),
         M2 * K2 * 2 + M2 * K2 // 2 + M2 * K2 // 32)
     # Q-row fused with its rowwise FP8 conversion (omo_per_token_group_quant_fp4_fused_ToFp8)
     f8q = torch.empty(M2, K2, dtype=torch.uint8, device=dev)
     f8s = torch.empty(K2 // 128, M2, dtype=torch.float32, device=dev)
-    res["quant_fused_fp8_config2"] = timeit(
+    timeit("quant_fused_fp8_config2",
         lambda: capi.call("mxb_per_token_group_quant_fp4_fused_ToFp8", x.data_ptr(), M2, K2, K2,
                           q.data_ptr(), s.data_ptr(), f8q.data_ptr(), f8s.data_ptr(), 32, 1e-10,
                           -6.0, 6.0, 0, sh),
         M2 * K2 * 2 + M2 * K2 // 2 + M2 * K2 // 32 + M2 * K2 + f8s.numel() * 4)
-    del x, q, s, f8q, f8s
+
+
+def _ops_config3(dev, sh, timeit, capi, syn):
+    import torch
     # config 3: codes [16384, 8192] u8 (K = 16384 elements), scales [16384, 512]
     c, sc = (t.to(dev) for t in syn.config3())
     M3, Kb3 = c.shape
     out = torch.empty(M3, 2 * Kb3, dtype=torch.bfloat16, device=dev)
-    res["dequant_bf16_config3"] = timeit(
+    timeit("dequant_bf16_config3",
         lambda: capi.call("mxb_per_token_Mxfp4ToBf16_dequant", c.data_ptr(), sc.data_ptr(), M3, Kb3,
                           out.data_ptr(), sh), M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 4)
     del out
     f8 = torch.empty(M3, 2 * Kb3, dtype=torch.uint8, device=dev)
     fs = torch.empty(Kb3 // 64, M3, dtype=torch.float32, device=dev)
-    res["mxfp4_to_fp8_rows_config3"] = timeit(
+    timeit("mxfp4_to_fp8_rows_config3",
         lambda: capi.call("mxb_per_token_Mxfp4ToFp8", c.data_ptr(), sc.data_ptr(), M3, Kb3,
                           f8.data_ptr(), fs.data_ptr(), sh),
         M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + (Kb3 // 64) * M3 * 4)
     del fs
     fcs = torch.empty(M3 // 128, 2 * Kb3, dtype=torch.float32, device=dev)
-    res["mxfp4_to_fp8_col_config3"] = timeit(
+    timeit("mxfp4_to_fp8_col_config3",
         lambda: capi.call("mxb_per_token_Mxfp4ToFp8_col", c.data_ptr(), sc.data_ptr(), M3, Kb3,
                           f8.data_ptr(), fcs.data_ptr(), sh),
         M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fcs.numel() * 4)
-    res["mxfp4_to_fp8_colT_config3"] = timeit(
+    timeit("mxfp4_to_fp8_colT_config3",
         lambda: capi.call("mxb_per_token_Mxfp4RowToBf16ToFp8Col", c.data_ptr(), sc.data_ptr(), M3,
                           2 * Kb3, f8.data_ptr(), fcs.data_ptr(), 1e-10, sh),
         M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fcs.numel() * 4)
@@ -456,26 +489,28 @@ def time_other_ops(dev, stream, peak):
     i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
     dm, dso, dsco = i32(m_splits), i32(so), i32(sco)
     fss = torch.empty(accs, 2 * Kb3, dtype=torch.float32, device=dev)
-    res["mxfp4_to_fp8_colT_msplit8_config3"] = timeit(
+    timeit("mxfp4_to_fp8_colT_msplit8_config3",
         lambda: capi.call("mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit", c.data_ptr(),
                           sc.data_ptr(), M3, 2 * Kb3, f8.data_ptr(), fss.data_ptr(),
                           dm.data_ptr(), dso.data_ptr(), dsco.data_ptr(), len(m_splits),
                           max(m_splits), 1e-10, sh),
         M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fss.numel() * 4)
-    del c, sc, f8, fcs, fss
+
+
+def _ops_config4(dev, sh, timeit, capi, syn):
+    import torch
     # config 4 per-token FP8
     x4 = syn.config4().to(dev)
     M4, K4 = x4.shape
     q4 = torch.empty(M4, K4, dtype=torch.uint8, device=dev)
     s4 = torch.empty(M4, dtype=torch.float32, device=dev)
     alg4 = M4 * K4 * 2 + M4 * K4 + M4 * 4
-    res["fp8_quant_config4"] = timeit(
+    timeit("fp8_quant_config4",
         lambda: capi.call("mxb_per_token_quant_fp8", x4.data_ptr(), M4, K4, q4.data_ptr(),
                           s4.data_ptr(), 1e-10, sh), alg4)
-    res["fp8_dequant_config4"] = timeit(
+    timeit("fp8_dequant_config4",
         lambda: capi.call("mxb_per_token_dequant_fp8", q4.data_ptr(), s4.data_ptr(), M4, K4,
                           x4.data_ptr(), sh), alg4)
-    return res
 
 
 def _json_only_stdout():
