@@ -426,6 +426,8 @@ def time_other_ops(dev, stream, peak, only=None):
         _ops_config3(dev, sh, timeit, capi, syn)
     if want("fp8_quant_config4", "fp8_dequant_config4"):
         _ops_config4(dev, sh, timeit, capi, syn)
+    if want("moe_permute_wire_config5"):
+        _ops_permute(dev, sh, timeit, capi, syn)
     return res
 
 
@@ -495,6 +497,23 @@ def _ops_config3(dev, sh, timeit, capi, syn):
                           dm.data_ptr(), dso.data_ptr(), dsco.data_ptr(), len(m_splits),
                           max(m_splits), 1e-10, sh),
         M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fss.numel() * 4)
+
+
+def _ops_permute(dev, sh, timeit, capi, syn):
+    import torch
+    # MoE permute of received wire rows (config 5 shape: 4096 tokens x H = 7168, top-8,
+    # every (token, k) to its own expert slot): one read per row, eight row writes
+    T, H, k = 4096, 7168, 8
+    g = torch.Generator().manual_seed(5)
+    wire = torch.randint(0, 256, (T, 17 * H // 32), generator=g, dtype=torch.uint8).to(dev)
+    dst = torch.randperm(T * k, generator=g).to(torch.int32).reshape(T, k).to(dev)
+    oc = torch.empty(T * k, H // 2, dtype=torch.uint8, device=dev)
+    os_ = torch.empty(T * k, H // 32, dtype=torch.uint8, device=dev)
+    timeit("moe_permute_wire_config5",
+           lambda: capi.call("mxb_moe_permute_mxfp4", wire.data_ptr(), 17 * H // 32,
+                             wire.data_ptr() + H // 2, 17 * H // 32, T, H, dst.data_ptr(), k,
+                             oc.data_ptr(), os_.data_ptr(), T * k, sh),
+           T * 17 * H // 32 + T * k * 17 * H // 32 + T * k * 4)
 
 
 def _ops_config4(dev, sh, timeit, capi, syn):

@@ -216,6 +216,20 @@ mxb_status mxb_ep_unpack(const void* wire, int64_t R, int64_t H, const float* we
 mxb_status mxb_ep_combine(const void* recv, int64_t T, int64_t H, const int32_t* slots, int G,
                           void* out, mxb_stream_t stream);
 
+/* MoE permute of MXFP4 rows (the MXFP4 branch of Transformer Engine's moe_permute,
+ * transformer_engine-2.8.diff:253-261,338-356), fused with the EP receive split:
+ * source row i (codes at codes + i*codes_pitch, H/2 bytes; E8M0 scales at
+ * scales + i*scales_pitch, H/32 bytes; wire rows: scales = codes + H/2 and both
+ * pitches 17H/32) is copied to output rows dst[i*topk + k] of out_codes
+ * [n_out, H/2] and out_scales [n_out, H/32] for k < topk; destinations outside
+ * [0, n_out) (e.g. -1) are skipped.  dst: int32 DEVICE [rows, topk], topk <= 32.
+ * The caller derives dst from its routing map (TE's row_id_map, DeepEP's
+ * handle); each row is read once whatever topk is. */
+mxb_status mxb_moe_permute_mxfp4(const void* codes, int64_t codes_pitch, const void* scales,
+                                 int64_t scales_pitch, int64_t rows, int64_t H, const int32_t* dst,
+                                 int topk, void* out_codes, void* out_scales, int64_t n_out,
+                                 mxb_stream_t stream);
+
 /* ---- fused dispatch / combine over NVLink peer memory ----
  * One buffer per rank with the layout below, mapped into every peer with CUDA
  * IPC (mxb_ipc_export / mxb_ipc_import); `bases` is a DEVICE array of the world

@@ -15,6 +15,8 @@
 //    summed in rank order (deterministic).
 #include <cuda_bf16.h>
 
+#include <type_traits>
+
 #include "capi_util.h"
 #include "common.cuh"
 
@@ -180,6 +182,64 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(const uint8_t* _
 
 int ep_grid(int64_t rows) { return (int)(rows < 148LL * 16 ? (rows > 0 ? rows : 1) : 148LL * 16); }
 
+// ------------------------------------------------------------ moe_permute
+// The MXFP4 branch of Transformer Engine's moe_permute (transformer_engine-2.8.diff:
+// 253-261,338-356): every source row goes, codes and E8M0 scales alike, to each
+// expert slot it is routed to.  Here fused with the EP receive side: the source
+// rows may be wire rows (codes || scales, megatron-0.15.0rc7.diff:32-63), which
+// are split in the same pass.  One warp per source row reads the row once
+// (16-byte chunks when every address and pitch allows, else 4-byte words, else
+// bytes) and
+// stores it to each destination dst[i * topk + k] in [0, n_out); other values
+// (e.g. -1 for no slot) are skipped.
+constexpr int kPermWarps = kEpThreads / 32;
+
+template <int kVec>
+__device__ __forceinline__ void permute_span(const uint8_t* src, int64_t bytes, uint8_t* out,
+                                             int64_t out_pitch, const int32_t (&d)[32], int topk,
+                                             int64_t n_out, int lane) {
+  using V = typename std::conditional<
+      kVec == 16, uint4, typename std::conditional<kVec == 4, uint32_t, uint8_t>::type>::type;
+  constexpr int kBatch = 8;  // chunks per lane loaded before any is stored
+  const int64_t n = bytes / kVec;
+  for (int64_t c0 = 0; c0 < n; c0 += 32 * kBatch) {
+    V v[kBatch];
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const int64_t c = c0 + b * 32 + lane;
+      if (c < n) v[b] = *reinterpret_cast<const V*>(src + c * kVec);
+    }
+    for (int k = 0; k < topk; ++k) {
+      const int32_t dk = d[k];
+      if (dk < 0 || dk >= n_out) continue;
+      uint8_t* o = out + (int64_t)dk * out_pitch;
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int64_t c = c0 + b * 32 + lane;
+        if (c < n) *reinterpret_cast<V*>(o + c * kVec) = v[b];
+      }
+    }
+  }
+}
+
+template <int kVec>
+__global__ void __launch_bounds__(kEpThreads) moe_permute_kernel(
+    const uint8_t* __restrict__ codes, int64_t cpitch, const uint8_t* __restrict__ scales,
+    int64_t spitch, int64_t rows, int64_t H, const int32_t* __restrict__ dst, int topk,
+    uint8_t* __restrict__ out_codes, uint8_t* __restrict__ out_scales, int64_t n_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (int64_t)blockIdx.x * kPermWarps + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * kPermWarps;
+  for (int64_t i = warp0; i < rows; i += nwarps) {
+    const int32_t mine = lane < topk ? dst[i * topk + lane] : -1;
+    int32_t d[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) d[k] = __shfl_sync(0xffffffffu, mine, k);
+    permute_span<kVec>(codes + i * cpitch, H / 2, out_codes, H / 2, d, topk, n_out, lane);
+    permute_span<kVec>(scales + i * spitch, H / 32, out_scales, H / 32, d, topk, n_out, lane);
+  }
+}
+
 }  // namespace
 }  // namespace mxb
 
@@ -226,4 +286,37 @@ extern "C" mxb_status mxb_ep_combine(const void* recv, int64_t T, int64_t H, con
   ep_combine_kernel<<<ep_grid(T), kEpThreads, 0, to_cuda(stream)>>>(
       (const uint8_t*)recv, T, H, slots, G, (uint8_t*)out);
   return launch_status("ep_combine");
+}
+
+extern "C" mxb_status mxb_moe_permute_mxfp4(const void* codes, int64_t codes_pitch,
+                                            const void* scales, int64_t scales_pitch, int64_t rows,
+                                            int64_t H, const int32_t* dst, int topk,
+                                            void* out_codes, void* out_scales, int64_t n_out,
+                                            mxb_stream_t stream) {
+  MXB_REQUIRE(rows >= 0 && H > 0 && H % 32 == 0 && topk >= 1 && topk <= 32 && n_out >= 0,
+              MXB_ERR_INVALID_ARGUMENT, "moe_permute_mxfp4: need H %% 32 == 0 and 1 <= topk <= 32");
+  MXB_REQUIRE(codes_pitch >= H / 2 && scales_pitch >= H / 32, MXB_ERR_INVALID_ARGUMENT,
+              "moe_permute_mxfp4: pitches must cover a row (codes H/2, scales H/32 bytes)");
+  if (rows == 0 || n_out == 0) return MXB_OK;
+  MXB_REQUIRE(codes && scales && dst && out_codes && out_scales, MXB_ERR_INVALID_ARGUMENT,
+              "moe_permute_mxfp4: null pointer");
+  const uintptr_t any = reinterpret_cast<uintptr_t>(codes) | reinterpret_cast<uintptr_t>(scales) |
+                        reinterpret_cast<uintptr_t>(out_codes) |
+                        reinterpret_cast<uintptr_t>(out_scales) | (uintptr_t)codes_pitch |
+                        (uintptr_t)scales_pitch | (uintptr_t)(H / 2) | (uintptr_t)(H / 32);
+  const int64_t warps_needed = rows;
+  const int grid = (int)min((int64_t)148 * 8, cdiv(warps_needed, kPermWarps));
+  if ((any & 15) == 0)
+    moe_permute_kernel<16><<<grid, kEpThreads, 0, to_cuda(stream)>>>(
+        (const uint8_t*)codes, codes_pitch, (const uint8_t*)scales, scales_pitch, rows, H, dst,
+        topk, (uint8_t*)out_codes, (uint8_t*)out_scales, n_out);
+  else if ((any & 3) == 0)
+    moe_permute_kernel<4><<<grid, kEpThreads, 0, to_cuda(stream)>>>(
+        (const uint8_t*)codes, codes_pitch, (const uint8_t*)scales, scales_pitch, rows, H, dst,
+        topk, (uint8_t*)out_codes, (uint8_t*)out_scales, n_out);
+  else
+    moe_permute_kernel<1><<<grid, kEpThreads, 0, to_cuda(stream)>>>(
+        (const uint8_t*)codes, codes_pitch, (const uint8_t*)scales, scales_pitch, rows, H, dst,
+        topk, (uint8_t*)out_codes, (uint8_t*)out_scales, n_out);
+  return launch_status("moe_permute_mxfp4");
 }

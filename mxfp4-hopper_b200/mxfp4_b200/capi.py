@@ -39,6 +39,7 @@ SIGNATURES = {
     "mxb_ep_pack": [_P, _I64, _I64, _P, _I, _P, _F, _P],
     "mxb_ep_unpack": [_P, _I64, _I64, _P, _P, _P],
     "mxb_ep_combine": [_P, _I64, _I64, _P, _I, _P, _P],
+    "mxb_moe_permute_mxfp4": [_P, _I64, _P, _I64, _I64, _I64, _P, _I, _P, _P, _I64, _P],
 }
 
 class EpLayout(ctypes.Structure):

@@ -10,6 +10,7 @@ import torch
 import torch.multiprocessing as mp
 
 from ep_oracle import combine_rows, expected_round, pack_rows, unpack_rows
+from mxfp4_b200 import capi
 from mxfp4_b200 import synthetic as syn
 from mxfp4_b200.ep import CudaKernels, build_route, weight_sums
 
@@ -121,3 +122,46 @@ def test_dispatch_combine_nccl():
         p.join(timeout=60)
     for rank, ok in sorted(res):
         assert ok is True, f"rank {rank}: {ok}"
+
+
+# ------------------------------------------------------------------ moe_permute
+def _permute_ref(codes, scales, dst, n_out, fill=0x5A):
+    """out[dst[i, k]] = row i (codes and scales), destinations outside [0, n_out) skipped."""
+    rows, topk = dst.shape
+    oc = np.full((n_out, codes.shape[1]), fill, np.uint8)
+    os_ = np.full((n_out, scales.shape[1]), fill, np.uint8)
+    for i in range(rows):
+        for k in range(topk):
+            d = int(dst[i, k])
+            if 0 <= d < n_out:
+                oc[d] = codes[i]
+                os_[d] = scales[i]
+    return oc, os_
+
+
+@pytest.mark.parametrize("rows,H,topk,wire", [(300, 7168, 8, True), (300, 7168, 8, False),
+                                               (77, 128, 3, True), (5, 64, 1, False),
+                                               (9, 96, 2, True)])
+def test_moe_permute_mxfp4(cuda, rows, H, topk, wire):
+    g = np.random.default_rng(rows + H + topk)
+    codes = g.integers(0, 256, (rows, H // 2), dtype=np.uint8)
+    scales = g.integers(100, 150, (rows, H // 32), dtype=np.uint8)
+    n_out = rows * topk - (rows * topk) // 8 - 1
+    dst = g.permutation(rows * topk).astype(np.int32).reshape(rows, topk)
+    dst[dst >= n_out] = -1            # a few routed-nowhere slots
+    dst[0, 0] = -1
+    oc_ref, os_ref = _permute_ref(codes, scales, dst, n_out)
+    if wire:  # EP receive rows: codes || scales, pitch 17H/32
+        src = torch.from_numpy(np.concatenate([codes, scales], axis=1)).to(cuda)
+        cptr, cp, sptr, sp = src.data_ptr(), 17 * H // 32, src.data_ptr() + H // 2, 17 * H // 32
+    else:
+        c_d, s_d = torch.from_numpy(codes).to(cuda), torch.from_numpy(scales).to(cuda)
+        cptr, cp, sptr, sp = c_d.data_ptr(), H // 2, s_d.data_ptr(), H // 32
+    d_d = torch.from_numpy(dst).to(cuda)
+    oc = torch.full((n_out, H // 2), 0x5A, dtype=torch.uint8, device=cuda)
+    os_ = torch.full((n_out, H // 32), 0x5A, dtype=torch.uint8, device=cuda)
+    capi.call("mxb_moe_permute_mxfp4", cptr, cp, sptr, sp, rows, H, d_d.data_ptr(), topk,
+              oc.data_ptr(), os_.data_ptr(), n_out, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(oc.cpu().numpy(), oc_ref)
+    np.testing.assert_array_equal(os_.cpu().numpy(), os_ref)
