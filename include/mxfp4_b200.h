@@ -94,6 +94,25 @@ mxb_status mxb_quant_mxfp4_rowcol(const void* input, int64_t M, int64_t K, int64
                                   void* scales_col, void* scales_row_swizzled, float eps,
                                   float fp4_min, float fp4_max, mxb_stream_t stream);
 
+/* mxb_quant_mxfp4_rowcol on HOST buffers (the end-to-end call for data in host
+ * memory; pinned memory for full speed): x_host bf16 [M, K] -> codes_row_host
+ * [M, K/2], scales_row_host [M, K/32], codes_col_host [K, M/2], scales_col_host
+ * [K, M/32], the same bytes as the device call.  Row chunks of chunk_rows
+ * (a multiple of 128; 0 picks 1024) are pipelined: chunk i's host->device copy,
+ * chunk i-1's quantize on `stream` and chunk i-2's device->host copies overlap,
+ * on two internal copy streams per device.  workspace: DEVICE memory, 256-byte
+ * aligned, of mxb_quant_mxfp4_rowcol_host_workspace(M, K, chunk_rows) bytes,
+ * for two chunks in flight; nothing is allocated.  Asynchronous: the outputs are
+ * complete when `stream` reaches the point after this call.  No reference
+ * counterpart (the reference works on device tensors only). */
+mxb_status mxb_quant_mxfp4_rowcol_host(const void* x_host, int64_t M, int64_t K,
+                                       void* codes_row_host, void* scales_row_host,
+                                       void* codes_col_host, void* scales_col_host,
+                                       void* workspace, int64_t workspace_bytes,
+                                       int64_t chunk_rows, float eps, float fp4_min,
+                                       float fp4_max, mxb_stream_t stream);
+int64_t mxb_quant_mxfp4_rowcol_host_workspace(int64_t M, int64_t K, int64_t chunk_rows);
+
 /* Rewrites row-major E8M0 scales [M, S] into the 128x4-tile swizzled layout
  * [round_up(M,128), round_up(S,4)] (zero padding).  Shape rule from
  * MXFP4Quantizer.get_scale_shape (code/transformer_engine-2.8.diff:752-786). */

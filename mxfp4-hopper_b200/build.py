@@ -30,7 +30,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
               "--expt-relaxed-constexpr", f"-I{INC}", f"-I{CSRC}"] + ARCH
 CU_SOURCES = ["quantize.cu", "dequant.cu", "convert_col.cu", "fp8_token.cu", "ep.cu", "ep_p2p.cu"]
-CPP_SOURCES = ["capi_util.cpp"]
+CPP_SOURCES = ["capi_util.cpp", "host_pipeline.cpp"]
 
 
 def _nvcc() -> str:

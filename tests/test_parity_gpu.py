@@ -115,6 +115,27 @@ def test_quant_rows_generic_params(cuda, orc, eps, fmin, fmax):
     H.assert_bytes_equal(H.np_u8(q), rq, "codes")
 
 
+# -------------------------------------------- rowcol on host buffers (pipelined)
+@pytest.mark.parametrize("M,K,chunk", [(4192, 1024, 512), (4096, 512, 0), (96, 256, 128)])
+def test_quant_rowcol_host(cuda, M, K, chunk):
+    """The host-buffer entry point equals the device call byte for byte, including a
+    partial last chunk (M not a multiple of chunk_rows)."""
+    from mxfp4_b200 import capi
+    x = syn.config2(M, K, seed=17)
+    cr, sr, cc, sc, _ = H.quant_rowcol(x.to(cuda))
+    xh = x.pin_memory()
+    outs = [torch.full(tuple(t.shape), 0x77, dtype=torch.uint8).pin_memory() for t in (cr, sr, cc, sc)]
+    L = capi.load()
+    wb = int(L.mxb_quant_mxfp4_rowcol_host_workspace(M, K, chunk))
+    ws = torch.empty(wb, dtype=torch.uint8, device=cuda)
+    capi.call("mxb_quant_mxfp4_rowcol_host", xh.data_ptr(), M, K, *[t.data_ptr() for t in outs],
+              ws.data_ptr(), wb, chunk, 1e-10, -6.0, 6.0, H.stream())
+    torch.cuda.synchronize()
+    for got, want, what in zip(outs, (cr, sr, cc, sc), ("codes_row", "scales_row", "codes_col",
+                                                        "scales_col")):
+        H.assert_bytes_equal(got.numpy(), H.np_u8(want), what)
+
+
 # -------------------------------------------- fused Q-row + rowwise FP8
 def _fused_cases():
     x = syn.config1(64, 1024, seed=8)
