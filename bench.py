@@ -424,7 +424,7 @@ def time_other_ops(dev, stream, peak, only=None):
     C3 = ("dequant_bf16_config3", "mxfp4_to_fp8_rows_config3", "mxfp4_to_fp8_col_config3",
           "mxfp4_to_fp8_colT_config3", "mxfp4_to_fp8_colT_msplit8_config3")
     # Q-row alone on config 2
-    if want("quant_rows_config2", "quant_fused_fp8_config2"):
+    if want("quant_rows_config2", "quant_fused_fp8_config2", "swiglu_quant_config2"):
         _ops_config2(dev, sh, timeit, capi, syn)
     if want(*C3):
         _ops_config3(dev, sh, timeit, capi, syn)
@@ -447,6 +447,13 @@ def _ops_config2(dev, sh, timeit, capi, syn):
     # Q-row fused with its rowwise FP8 conversion (omo_per_token_group_quant_fp4_fused_ToFp8)
     f8q = torch.empty(M2, K2, dtype=torch.uint8, device=dev)
     f8s = torch.empty(K2 // 128, M2, dtype=torch.float32, device=dev)
+    # Megatron SwiGLU with fp4_input_store: config 2's tensor as the [M, 2H] input
+    yq = torch.empty(M2, K2 // 2, dtype=torch.bfloat16, device=dev)
+    timeit("swiglu_quant_config2",
+           lambda: capi.call("mxb_swiglu_quant_mxfp4", x.data_ptr(), M2, K2 // 2, yq.data_ptr(),
+                             q.data_ptr(), s.data_ptr(), 1e-10, -6.0, 6.0, sh),
+           M2 * K2 * 2 + M2 * K2 // 2 * 2 + M2 * K2 // 2 + M2 * K2 // 32)
+    del yq
     timeit("quant_fused_fp8_config2",
         lambda: capi.call("mxb_per_token_group_quant_fp4_fused_ToFp8", x.data_ptr(), M2, K2, K2,
                           q.data_ptr(), s.data_ptr(), f8q.data_ptr(), f8s.data_ptr(), 32, 1e-10,

@@ -78,6 +78,17 @@ mxb_status mxb_per_token_group_quant_fp4_fused_ToFp8(const void* input, int64_t 
                                                      float fp4_max, int scale_ue8m0,
                                                      mxb_stream_t stream);
 
+/* Megatron's SwiGLU with fp4_input_store in one pass (megatron-0.15.0rc7.diff:
+ * 164-193, next row 4 of the path): input bf16 [M, 2H] -> output bf16 [M, H] =
+ * silu(x[:, :H]) * x[:, H:] (f32, one rounding to BF16), and the rowwise MXFP4
+ * of the input itself, codes [M, H] (= 2H/2) and E8M0 scales [M, H/16] (=
+ * 2H/32), bit-identical to mxb_per_token_group_quant_fp4 on the input.  H % 32
+ * == 0.  No reference counterpart as one kernel (the reference runs the
+ * quantizer and the activation separately). */
+mxb_status mxb_swiglu_quant_mxfp4(const void* input, int64_t M, int64_t H, void* output,
+                                  void* codes, void* scales, float eps, float fp4_min,
+                                  float fp4_max, mxb_stream_t stream);
+
 /* Rowwise AND columnwise BF16 -> MXFP4 in one pass over the input.
  * Replaces the Transformer Engine quantize of the reference
  * (code/transformer_engine-2.8.diff:1464-1466): rowwise = Q-row of input,

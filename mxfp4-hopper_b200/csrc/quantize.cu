@@ -527,6 +527,92 @@ bool fast_params(float eps, float fp4_min, float fp4_max) {
   return fp4_max == 6.0f && fp4_min == -6.0f && eps >= 0.0f && eps <= 6e-10f;
 }
 
+// ------------------------------------------------- SwiGLU fused with Q-row
+// Megatron's SwiGLU with fp4_input_store (megatron-0.15.0rc7.diff:164-193)
+// returns swiglu(x) = silu(x1) * x2 (x1, x2 the two halves of the last
+// dimension) and keeps the MXFP4 quantization of x itself for the backward
+// pass.  One pass reads x once and writes both: lane pairs own the gate block
+// j (elements 32j..32j+31) and the up block j (H + 32j ..) of a row, quantize
+// both exactly as Q-row does, and form 16 outputs each.  silu(g) * u is
+// evaluated in f32 and rounded to BF16 once.
+template <bool kFast>
+__global__ void __launch_bounds__(256) swiglu_quant_kernel(const __nv_bfloat16* __restrict__ x,
+                                                           int64_t M, int64_t H,
+                                                           __nv_bfloat16* __restrict__ y,
+                                                           uint8_t* __restrict__ codes,
+                                                           uint8_t* __restrict__ scales,
+                                                           QuantParams p) {
+  const int64_t J = H >> 5;        // block pairs per row
+  const int64_t halves = M * J * 2;
+  const int lane = threadIdx.x & 31;
+  const unsigned pair_mask = 3u << (lane & ~1);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t K = 2 * H;         // row length of x
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < halves;
+       base += stride) {
+    const int64_t h = base + lane;
+    if (h >= halves) continue;  // pairs are both in or both out (halves is even)
+    const int64_t pr = h >> 1;
+    const int half = (int)(h & 1);
+    const int64_t r = pr / J, j = pr - r * J;
+    uint32_t wv[2][8];  // [gate, up][16 elements as BF16 pairs]
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const uint8_t* src =
+          reinterpret_cast<const uint8_t*>(x + r * K + s * H + j * 32 + half * 16);
+      const uint4 a = ld_stream_v4(src), b = ld_stream_v4(src + 16);
+      wv[s][0] = a.x; wv[s][1] = a.y; wv[s][2] = a.z; wv[s][3] = a.w;
+      wv[s][4] = b.x; wv[s][5] = b.y; wv[s][6] = b.z; wv[s][7] = b.w;
+    }
+    // ---- MXFP4 of both blocks (bit-exact Q-row)
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const uint32_t (&w)[8] = wv[s];
+      uint32_t mb = max_abs_pairs(w);
+      mb = max(mb, __shfl_xor_sync(pair_mask, mb, 1));
+      uint32_t byte, out[2];
+      if (kFast && mb < 0x7F80u) {
+        uint32_t inv;
+        scale_fast(mb, byte, inv);
+        out[0] = encode8_pairs(&w[0], inv);
+        out[1] = encode8_pairs(&w[4], inv);
+      } else {
+        uint32_t f0[8], f1[8];
+        unpack8(&w[0], f0);
+        unpack8(&w[4], f1);
+        float am = fmaxf(amax_generic(f0, p.eps), amax_generic(f1, p.eps));
+        am = fmaxf(am, __shfl_xor_sync(pair_mask, am, 1));
+        float inv;
+        scale_generic(am, p, inv, byte);
+        out[0] = encode8_generic(f0, inv, p);
+        out[1] = encode8_generic(f1, inv, p);
+      }
+      const int64_t blk = s * J + j;  // block index within the row of x
+      st_stream_v2(codes + r * H + blk * 16 + half * 8, make_uint2(out[0], out[1]));
+      if (half == 0) scales[r * (2 * J) + blk] = (uint8_t)byte;
+    }
+    // ---- swiglu of the 16 (gate, up) pairs
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float v[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float g = e ? bf16hi_to_f(wv[0][i]) : bf16lo_to_f(wv[0][i]);
+        const float u = e ? bf16hi_to_f(wv[1][i]) : bf16lo_to_f(wv[1][i]);
+        // g * u * (1 / (1 + e^-g)): the hardware exponential and a correctly
+        // rounded reciprocal keep the relative error near 1e-6, far inside one
+        // BF16 ulp; e^-g = Inf gives (g * u) * +0, keeping the sign of zero
+        v[e] = (g * u) * __frcp_rn(1.0f + __expf(-g));
+      }
+      o[i] = cvt_bf16x2(v[0], v[1]);
+    }
+    uint8_t* dst = reinterpret_cast<uint8_t*>(y + r * H + j * 32 + half * 16);
+    st_stream_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
+    st_stream_v4(dst + 16, make_uint4(o[4], o[5], o[6], o[7]));
+  }
+}
+
 template <bool kFp8>
 void launch_quant_rows(bool fast, const void* input, int64_t M, int64_t K, int64_t ldx,
                        void* output_q, void* output_s, const QuantParams& p, void* fp8, void* fp8_s,
@@ -602,6 +688,34 @@ extern "C" mxb_status mxb_per_token_group_quant_fp4_fused_ToFp8(
   launch_quant_rows<true>(fast_params(eps, fp4_min, fp4_max), input, M, K, ldx, output_q, output_s,
                           p, output_fp8, output_fp8_s, stream);
   return launch_status("quant_fp4_fused_fp8");
+}
+
+extern "C" mxb_status mxb_swiglu_quant_mxfp4(const void* input, int64_t M, int64_t H, void* output,
+                                             void* codes, void* scales, float eps, float fp4_min,
+                                             float fp4_max, mxb_stream_t stream) {
+  MXB_REQUIRE(M >= 0 && H >= 0 && H % 32 == 0, MXB_ERR_INVALID_ARGUMENT,
+              "swiglu_quant: need H %% 32 == 0 (M=%lld H=%lld)", (long long)M, (long long)H);
+  if (M == 0 || H == 0) return MXB_OK;
+  MXB_REQUIRE(input && output && codes && scales, MXB_ERR_INVALID_ARGUMENT,
+              "swiglu_quant: null pointer");
+  MXB_REQUIRE(aligned(input, 16) && aligned(output, 16) && aligned(codes, 8), MXB_ERR_MISALIGNED,
+              "swiglu_quant: input and output must be 16-byte and codes 8-byte aligned");
+  const QuantParams p{eps, fp4_min, fp4_max};
+  const bool fast = fast_params(eps, fp4_min, fp4_max);
+  const void* kern = fast ? (const void*)swiglu_quant_kernel<true> : (const void*)swiglu_quant_kernel<false>;
+  const int64_t halves = M * (H / 32) * 2;
+  const int64_t want = cdiv(halves, 256);
+  const int64_t cap = (int64_t)persistent_ctas(kern, 256, 0) * 4;
+  const int grid = (int)(want < cap ? want : cap);
+  if (fast)
+    swiglu_quant_kernel<true><<<grid, 256, 0, to_cuda(stream)>>>(
+        (const __nv_bfloat16*)input, M, H, (__nv_bfloat16*)output, (uint8_t*)codes,
+        (uint8_t*)scales, p);
+  else
+    swiglu_quant_kernel<false><<<grid, 256, 0, to_cuda(stream)>>>(
+        (const __nv_bfloat16*)input, M, H, (__nv_bfloat16*)output, (uint8_t*)codes,
+        (uint8_t*)scales, p);
+  return launch_status("swiglu_quant");
 }
 
 extern "C" mxb_status mxb_quant_mxfp4_rowcol(const void* input, int64_t M, int64_t K, int64_t ldx,

@@ -26,6 +26,7 @@ SIGNATURES = {
                                                   _F, _F, _I, _P],
     "mxb_quant_mxfp4_rowcol_host": [_P, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _F, _F, _F,
                                     _P],
+    "mxb_swiglu_quant_mxfp4": [_P, _I64, _I64, _P, _P, _P, _F, _F, _F, _P],
     "mxb_swizzle_scales": [_P, _I64, _I64, _P, _P],
     "mxb_per_token_Mxfp4ToBf16_dequant": [_P, _P, _I64, _I64, _P, _P],
     "mxb_per_token_Mxfp4ToFp8": [_P, _P, _I64, _I64, _P, _P, _P],

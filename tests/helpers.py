@@ -54,6 +54,18 @@ def quant_fused_fp8(x, eps=1e-10, fmin=-6.0, fmax=6.0):
     return q, s, f, fs
 
 
+def swiglu_quant(x, eps=1e-10, fmin=-6.0, fmax=6.0):
+    """silu(x[:, :H]) * x[:, H:] and the rowwise MXFP4 of x, one launch."""
+    M, K = x.shape
+    Hh = K // 2
+    y = torch.empty(M, Hh, dtype=torch.bfloat16, device=x.device)
+    q = torch.empty(M, K // 2, dtype=torch.uint8, device=x.device)
+    s = torch.empty(M, K // 32, dtype=torch.uint8, device=x.device)
+    capi.call("mxb_swiglu_quant_mxfp4", dp(x), M, Hh, dp(y), dp(q), dp(s), eps, fmin, fmax,
+              stream())
+    return y, q, s
+
+
 def quant_rowcol(x, rows=True, swz=False, eps=1e-10, fmin=-6.0, fmax=6.0):
     M, K = x.shape
     dev = x.device

@@ -115,6 +115,34 @@ def test_quant_rows_generic_params(cuda, orc, eps, fmin, fmax):
     H.assert_bytes_equal(H.np_u8(q), rq, "codes")
 
 
+# -------------------------------------------- SwiGLU fused with Q-row
+@pytest.mark.parametrize("M,hid", [(64, 512), (3, 4096), (200, 7168)])
+def test_swiglu_quant(cuda, orc, M, hid):
+    """The MXFP4 of the input is bit-exact with Q-row; silu(g) * u (f32, one BF16
+    rounding) is within one BF16 ulp of torch's f32 evaluation."""
+    x = syn.config1(M, 2 * hid, seed=19)
+    y, q, s = H.swiglu_quant(x.to(cuda))
+    rq, rs = orc.quant_rows(_bits(x))
+    H.assert_bytes_equal(H.np_u8(s), rs, "scales")
+    H.assert_bytes_equal(H.np_u8(q), rq, "codes")
+    xf = x.float()
+    ref = (torch.nn.functional.silu(xf[:, :hid]) * xf[:, hid:]).to(torch.bfloat16)
+    a = H.np_u16(y).astype(np.int32)
+    b = H.np_u16(ref).astype(np.int32)
+    # same-sign BF16 patterns: ulp distance is the integer difference
+    assert np.abs(a - b).max() <= 1, f"max ulp difference {np.abs(a - b).max()}"
+
+
+def test_swiglu_quant_special_values(cuda, orc):
+    """Quantization of Inf / NaN / subnormal / tie inputs through the fused kernel."""
+    sp = special_block_input()
+    xb = np.concatenate([sp, sp[:, ::-1]], axis=1)  # 2H = 128
+    y, q, s = H.swiglu_quant(to_dev_bf16(xb, cuda))
+    rq, rs = orc.quant_rows(xb)
+    H.assert_bytes_equal(H.np_u8(s), rs, "scales")
+    H.assert_bytes_equal(H.np_u8(q), rq, "codes")
+
+
 # -------------------------------------------- rowcol on host buffers (pipelined)
 @pytest.mark.parametrize("M,K,chunk", [(4192, 1024, 512), (4096, 512, 0), (96, 256, 128)])
 def test_quant_rowcol_host(cuda, M, K, chunk):
