@@ -208,6 +208,19 @@ mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit_noalloc(
     void* output_s, const int32_t* m_splits, int64_t num_splits, int64_t max_split_len, float eps,
     mxb_stream_t stream);
 
+/* ------------------------------------------------------------ MXFP4 GEMM */
+
+/* No reference counterpart (the consumer of the quantized operands: next row 3
+ * of the path).  C bf16 [M, N] = A . B^T on the tcgen05 tensor cores
+ * (kind::mxf4 block_scale, f32 accumulation): A codes [M, K/2] and B codes
+ * [N, K/2] as mxb_per_token_group_quant_fp4 writes them, their E8M0 scales in
+ * the 128x4-tile swizzled layout of mxb_swizzle_scales ([M, K/32] -> [M, K/32]
+ * for M % 128 == 0 and K % 128 == 0).  M % 128, N % 128, K % 256 == 0. */
+mxb_status mxb_gemm_mxfp4(const void* a_codes, const void* a_scales_swizzled, const void* b_codes,
+                          const void* b_scales_swizzled, int64_t M, int64_t N, int64_t K, void* c,
+                          mxb_stream_t stream);
+unsigned int mxb_gemm_wait_timeouts(void);
+
 /* ------------------------------------------------------------ per-token FP8 */
 
 /* BF16 -> FP8 E4M3 with one FP32 scale per row: amax = max(eps, max|x|),

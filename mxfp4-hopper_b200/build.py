@@ -29,7 +29,8 @@ BUILD = PKG / "_build"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
               "--expt-relaxed-constexpr", f"-I{INC}", f"-I{CSRC}"] + ARCH
-CU_SOURCES = ["quantize.cu", "dequant.cu", "convert_col.cu", "fp8_token.cu", "ep.cu", "ep_p2p.cu"]
+CU_SOURCES = ["quantize.cu", "dequant.cu", "convert_col.cu", "fp8_token.cu", "ep.cu", "ep_p2p.cu",
+              "gemm_mxfp4.cu"]
 CPP_SOURCES = ["capi_util.cpp", "host_pipeline.cpp"]
 
 

@@ -1,0 +1,270 @@
+// Block-scaled MXFP4 GEMM on the 5th-generation tensor cores (sm_100a): the
+// consumer on the far side of the quantize path.  C[M, N] (BF16) = A[M, K] .
+// B[N, K]^T where A and B are MXFP4 exactly as this library's rowwise quantize
+// writes them: E2M1 codes [rows, K/2] (element 2i in the low nibble) and E8M0
+// scales in the 128x4-tile swizzled layout of mxb_swizzle_scales /
+// scales_row_swizzled (the tcgen05 block-scale layout: a 512-byte atom holds
+// the 4 scales of 128 rows, row r at (r % 32) * 16 + (r / 32) * 4).
+//
+// One CTA computes one 128 x 128 tile of C; the K loop walks 256-element
+// steps.  Per step a single thread
+//   * lands the A and B tiles (128 rows x 128 bytes each) with TMA (128-byte
+//     swizzle) and the step's two scale atoms of A and of B (1 KiB each) with
+//     1-D bulk copies, all completing on one mbarrier;
+//   * copies each scale atom into tensor memory with tcgen05.cp (32 rows x 16
+//     bytes replicated to the four lane quadrants: 4 TMEM columns per atom);
+//   * issues four tcgen05.mma.kind::mxf4.block_scale.block32 (K = 64 each; the
+//     scale byte pair of a K-half is selected through the top two bits of the
+//     TMEM scale address) accumulating in TMEM (128 lanes x 128 f32 columns);
+//   * commits them to a second mbarrier before the next step reuses the tiles.
+// The four warps then read the accumulator with tcgen05.ld (warp w owns lanes
+// 32w .. 32w+31 = rows of C) and store BF16.  Descriptor formats follow the
+// Blackwell UMMA descriptors (CUTLASS cute/arch/mma_sm100_desc.hpp).  Every
+// wait is bounded; a CTA whose wait gives up records it, skips its stores and
+// still releases its tensor memory.
+#include <cuda_bf16.h>
+
+#include "capi_util.h"
+#include "common.cuh"
+#include "tma.cuh"
+
+namespace mxb {
+namespace {
+
+constexpr int kGemmThreads = 128;
+constexpr int kTileM = 128, kTileN = 128, kTileK = 256;   // elements
+constexpr uint32_t kTileBytes = 128 * 128;                 // 128 rows x 128 code bytes
+constexpr uint32_t kSfBytes = 2 * 512;                     // two 128x4 scale atoms per step
+constexpr uint32_t kTmemCols = 256;                        // accumulator 128 + scales
+constexpr uint32_t kAccCol = 0, kSfaCol = 128, kSfbCol = 136;
+// dynamic shared memory: tiles (1024-byte aligned for the swizzle), scale atoms,
+// barriers; sized so that at most two CTAs share an SM (2 x 256 TMEM columns)
+constexpr size_t kGemmSmem = 100 * 1024;
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
+  // K-major, 128-byte swizzle: 8-row atoms of 128-byte rows, SBO = 1024 B,
+  // LBO = 16 B (unused for swizzled K-major), version 1, layout type 2
+  const uint64_t a = (smem_addr(p) >> 4) & 0x3FFFu;
+  return a | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
+         (uint64_t(2) << 61);
+}
+
+__device__ __forceinline__ uint64_t smem_desc_sf(const void* p) {
+  // scale atom: 32 rows of 16 bytes, no swizzle: SBO = 128 B between 8-row
+  // core matrices, LBO = 512 B, version 1, layout type 0
+  const uint64_t a = (smem_addr(p) >> 4) & 0x3FFFu;
+  return a | (uint64_t(512 >> 4) << 16) | (uint64_t(128 >> 4) << 32) | (uint64_t(1) << 46);
+}
+
+// Instruction descriptor of kind::mxf4 block_scale: E2M1 x E2M1, E8M0 scales,
+// K-major A and B, M = 128, N = kTileN; sf ids in bits 4-5 (B) and 29-30 (A).
+__host__ __device__ constexpr uint32_t gemm_idesc(uint32_t a_sf_id, uint32_t b_sf_id) {
+  return (b_sf_id << 4) | (1u << 7) | (1u << 10) | (uint32_t(kTileN >> 3) << 17) | (1u << 23) |
+         (uint32_t(kTileM >> 4) << 24) | (a_sf_id << 29);
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_addr(dst)),
+               "r"(cols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_copy_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n}"
+      ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kGemmThreads) gemm_mxfp4_kernel(
+    const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+    const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, int64_t M, int64_t N,
+    int64_t K, __nv_bfloat16* __restrict__ c, unsigned int* __restrict__ timeouts) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sa = smem;                        // A tile, 16 KiB
+  uint8_t* sb = smem + kTileBytes;           // B tile, 16 KiB
+  uint8_t* ssfa = sb + kTileBytes;           // 2 scale atoms of A
+  uint8_t* ssfb = ssfa + kSfBytes;           // 2 scale atoms of B
+  uint64_t* bar_load = reinterpret_cast<uint64_t*>(ssfb + kSfBytes);
+  uint64_t* bar_mma = bar_load + 1;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  int* failed = reinterpret_cast<int*>(tmem_base_slot + 1);
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int64_t m0 = (int64_t)blockIdx.y * kTileM, n0 = (int64_t)blockIdx.x * kTileN;
+  const int64_t ksteps = K / kTileK;
+  const int64_t sp4_a = K / 128, sp4_b = K / 128;  // scale atoms per 128-row block
+
+  if (t == 0) {
+    mbar_init(bar_load, 1);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+    *failed = 0;
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_base_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_slot;
+
+  if (t == 0) {
+    bool ok = true;
+    int load_pending = -1;  // parity of a load this thread stopped waiting for
+    for (int64_t ks = 0; ks < ksteps && ok; ++ks) {
+      const uint32_t ph = (uint32_t)(ks & 1);
+      // the previous step's MMAs have finished reading the tiles
+      if (ks > 0) ok = mbar_wait(bar_mma, ph ^ 1u);
+      if (!ok) break;
+      mbar_arrive_expect_tx(bar_load, 2 * kTileBytes + 2 * kSfBytes);
+      tma_load_2d(sa, &tmap_a, (int32_t)(ks * kTileK / 2), (int32_t)m0, bar_load);
+      tma_load_2d(sb, &tmap_b, (int32_t)(ks * kTileK / 2), (int32_t)n0, bar_load);
+      bulk_load_1d(ssfa, sfa + ((m0 / 128) * sp4_a + ks * 2) * 512, kSfBytes, bar_load);
+      bulk_load_1d(ssfb, sfb + ((n0 / 128) * sp4_b + ks * 2) * 512, kSfBytes, bar_load);
+      ok = mbar_wait(bar_load, ph);
+      if (!ok) {
+        load_pending = (int)ph;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int a = 0; a < 2; ++a) {
+        tc_copy_sf(tmem + kSfaCol + 4 * a, smem_desc_sf(ssfa + a * 512));
+        tc_copy_sf(tmem + kSfbCol + 4 * a, smem_desc_sf(ssfb + a * 512));
+      }
+      const uint64_t da = smem_desc_sw128(sa), db = smem_desc_sw128(sb);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        // K-half j covers elements 64j .. 64j+63 of the step: atom j/2, scale
+        // bytes 2(j%2) .. 2(j%2)+1 of each row's 32-bit scale column
+        const uint32_t sf_id = (uint32_t)(j & 1) * 2u;
+        const uint32_t tsfa = (tmem + kSfaCol + 4 * (j >> 1)) | (sf_id << 30);
+        const uint32_t tsfb = (tmem + kSfbCol + 4 * (j >> 1)) | (sf_id << 30);
+        tc_mma(tmem + kAccCol, da + (uint64_t)(2 * j), db + (uint64_t)(2 * j),
+               gemm_idesc(sf_id, sf_id), tsfa, tsfb, (ks > 0 || j > 0) ? 1u : 0u);
+      }
+      tc_commit(bar_mma);
+    }
+    // the last commit: the accumulator is complete (or a wait gave up)
+    if (ok && ksteps > 0) ok = mbar_wait(bar_mma, (uint32_t)((ksteps - 1) & 1));
+    if (!ok) {
+      *failed = 1;
+      atomicAdd(timeouts, 1u);
+      // do not release the CTA while a requested copy may still land
+      if (load_pending >= 0) mbar_wait(bar_load, (uint32_t)load_pending);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  if (!*failed) {
+    // epilogue: warp w reads lanes 32w .. 32w+31 (rows), 16 columns at a time
+    const int64_t row = m0 + warp * 32 + lane;
+#pragma unroll 1
+    for (int c0 = 0; c0 < kTileN; c0 += 16) {
+      uint32_t v[16];
+      tmem_ld16(tmem + kAccCol + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+      tmem_ld_wait();
+      uint32_t o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = cvt_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+      if (row < M) {
+        uint8_t* dst = reinterpret_cast<uint8_t*>(c + row * N + n0 + c0);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(dst + 16) = make_uint4(o[4], o[5], o[6], o[7]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+}
+
+__device__ unsigned int g_gemm_timeouts;
+
+}  // namespace
+}  // namespace mxb
+
+using namespace mxb;
+
+extern "C" mxb_status mxb_gemm_mxfp4(const void* a_codes, const void* a_scales_swizzled,
+                                     const void* b_codes, const void* b_scales_swizzled,
+                                     int64_t M, int64_t N, int64_t K, void* c,
+                                     mxb_stream_t stream) {
+  MXB_REQUIRE(M >= 0 && N >= 0 && K >= 0 && M % kTileM == 0 && N % kTileN == 0 &&
+                  K % kTileK == 0,
+              MXB_ERR_INVALID_ARGUMENT,
+              "gemm_mxfp4: need M %% 128, N %% 128 and K %% 256 == 0 (M=%lld N=%lld K=%lld)",
+              (long long)M, (long long)N, (long long)K);
+  if (M == 0 || N == 0) return MXB_OK;
+  MXB_REQUIRE(a_codes && a_scales_swizzled && b_codes && b_scales_swizzled && c,
+              MXB_ERR_INVALID_ARGUMENT, "gemm_mxfp4: null pointer");
+  MXB_REQUIRE(aligned(a_codes, 16) && aligned(b_codes, 16) && aligned(a_scales_swizzled, 16) &&
+                  aligned(b_scales_swizzled, 16) && aligned(c, 16),
+              MXB_ERR_MISALIGNED, "gemm_mxfp4: operands must be 16-byte aligned");
+  MXB_REQUIRE(K > 0, MXB_ERR_INVALID_ARGUMENT, "gemm_mxfp4: K must be positive");
+  CUtensorMap ta, tb;
+  if (!make_tensor_map_2d(&ta, a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K / 2, K / 2, 128,
+                          128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tensor_map_2d(&tb, b_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K / 2, K / 2, 128,
+                          128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return MXB_ERR_CUDA;
+  static const bool attr_ok =
+      cudaFuncSetAttribute((const void*)gemm_mxfp4_kernel,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) == cudaSuccess;
+  MXB_REQUIRE(attr_ok, MXB_ERR_CUDA, "gemm_mxfp4: cannot reserve shared memory");
+  unsigned int* timeouts = nullptr;
+  MXB_REQUIRE(cudaGetSymbolAddress((void**)&timeouts, g_gemm_timeouts) == cudaSuccess, MXB_ERR_CUDA,
+              "gemm_mxfp4: cannot find the timeout counter");
+  const dim3 grid((unsigned)(N / kTileN), (unsigned)(M / kTileM));
+  gemm_mxfp4_kernel<<<grid, kGemmThreads, kGemmSmem, to_cuda(stream)>>>(
+      ta, tb, (const uint8_t*)a_scales_swizzled, (const uint8_t*)b_scales_swizzled, M, N, K,
+      (__nv_bfloat16*)c, timeouts);
+  return launch_status("gemm_mxfp4");
+}
+
+extern "C" unsigned int mxb_gemm_wait_timeouts(void) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_gemm_timeouts, sizeof(v));
+  return v;
+}

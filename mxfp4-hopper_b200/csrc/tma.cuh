@@ -82,6 +82,18 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// 1-D bulk copy of `bytes` contiguous bytes global -> shared, completion
+// signalled on `bar` (complete_tx).  Both addresses 16-byte aligned, bytes a
+// multiple of 16.
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes,
+                                             uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
 // 2-D tiled TMA store of a shared-memory box to global memory (bulk group).
 // Elements outside the tensor are not written.  The writing threads must have
 // executed fence_proxy_async_smem() and synchronised before this is issued.

@@ -27,6 +27,7 @@ SIGNATURES = {
     "mxb_quant_mxfp4_rowcol_host": [_P, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _F, _F, _F,
                                     _P],
     "mxb_swiglu_quant_mxfp4": [_P, _I64, _I64, _P, _P, _P, _F, _F, _F, _P],
+    "mxb_gemm_mxfp4": [_P, _P, _P, _P, _I64, _I64, _I64, _P, _P],
     "mxb_swizzle_scales": [_P, _I64, _I64, _P, _P],
     "mxb_per_token_Mxfp4ToBf16_dequant": [_P, _P, _I64, _I64, _P, _P],
     "mxb_per_token_Mxfp4ToFp8": [_P, _P, _I64, _I64, _P, _P, _P],
@@ -100,6 +101,7 @@ def load() -> ctypes.CDLL:
         L.mxb_version.restype = ctypes.c_char_p
         L.mxb_wait_timeouts.restype = ctypes.c_uint
         L.mxb_ep_wait_timeouts.restype = ctypes.c_uint
+        L.mxb_gemm_wait_timeouts.restype = ctypes.c_uint
         L.mxb_quant_mxfp4_rowcol_host_workspace.argtypes = [_I64, _I64, _I64]
         L.mxb_quant_mxfp4_rowcol_host_workspace.restype = ctypes.c_int64
         _lib = L
