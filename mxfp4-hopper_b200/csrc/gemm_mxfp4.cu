@@ -6,22 +6,25 @@
 // scales_row_swizzled (the tcgen05 block-scale layout: a 512-byte atom holds
 // the 4 scales of 128 rows, row r at (r % 32) * 16 + (r / 32) * 4).
 //
-// One CTA computes one 128 x 128 tile of C; the K loop walks 256-element
-// steps.  Per step a single thread
-//   * lands the A and B tiles (128 rows x 128 bytes each) with TMA (128-byte
-//     swizzle) and the step's two scale atoms of A and of B (1 KiB each) with
-//     1-D bulk copies, all completing on one mbarrier;
-//   * copies each scale atom into tensor memory with tcgen05.cp (32 rows x 16
-//     bytes replicated to the four lane quadrants: 4 TMEM columns per atom);
-//   * issues four tcgen05.mma.kind::mxf4.block_scale.block32 (K = 64 each; the
-//     scale byte pair of a K-half is selected through the top two bits of the
-//     TMEM scale address) accumulating in TMEM (128 lanes x 128 f32 columns);
-//   * commits them to a second mbarrier before the next step reuses the tiles.
-// The four warps then read the accumulator with tcgen05.ld (warp w owns lanes
-// 32w .. 32w+31 = rows of C) and store BF16.  Descriptor formats follow the
-// Blackwell UMMA descriptors (CUTLASS cute/arch/mma_sm100_desc.hpp).  Every
-// wait is bounded; a CTA whose wait gives up records it, skips its stores and
-// still releases its tensor memory.
+// One CTA computes a 128 x 256 tile of C as two 128 x 128 accumulators in
+// tensor memory that share the A tile; the K loop walks 256-element steps
+// through a 4-stage shared-memory ring:
+//   * warp 0 (one thread) lands each step's A tile (128 rows x 128 bytes), B
+//     tile (256 rows x 128 bytes) with TMA (128-byte swizzle) and the step's
+//     scale atoms (2 for A, 4 for B, 512 bytes each) with 1-D bulk copies,
+//     completing on full[s];
+//   * warp 1 (one thread) copies the scale atoms into the stage's own tensor
+//     memory columns with tcgen05.cp (32 rows x 16 bytes replicated to the four
+//     lane quadrants: 4 columns per atom), issues 8 tcgen05.mma.kind::mxf4.
+//     block_scale.block32 per step (4 K-halves of 64 x 2 accumulators; the
+//     scale byte pair of a K-half is selected by the top two bits of the TMEM
+//     scale address) and commits them to empty[s], which frees the stage when
+//     they have run; after the last step it commits to acc_full;
+//   * warps 2..5 read the accumulators with tcgen05.ld (warp w owns lane
+//     quadrant w % 4 = rows 32(w%4) .. +31) and store BF16.
+// Descriptor formats follow the Blackwell UMMA descriptors (CUTLASS
+// cute/arch/mma_sm100_desc.hpp).  Every wait is bounded; a CTA whose wait gives
+// up records it, skips its stores and still releases its tensor memory.
 #include <cuda_bf16.h>
 
 #include "capi_util.h"
@@ -31,15 +34,19 @@
 namespace mxb {
 namespace {
 
-constexpr int kGemmThreads = 128;
-constexpr int kTileM = 128, kTileN = 128, kTileK = 256;   // elements
-constexpr uint32_t kTileBytes = 128 * 128;                 // 128 rows x 128 code bytes
-constexpr uint32_t kSfBytes = 2 * 512;                     // two 128x4 scale atoms per step
-constexpr uint32_t kTmemCols = 256;                        // accumulator 128 + scales
-constexpr uint32_t kAccCol = 0, kSfaCol = 128, kSfbCol = 136;
-// dynamic shared memory: tiles (1024-byte aligned for the swizzle), scale atoms,
-// barriers; sized so that at most two CTAs share an SM (2 x 256 TMEM columns)
-constexpr size_t kGemmSmem = 100 * 1024;
+constexpr int kGemmThreads = 192;                         // producer, MMA, 4 epilogue warps
+constexpr int kTileM = 128, kTileN = 256, kTileK = 256;   // elements
+constexpr int kHalfN = 128;                               // one accumulator / one MMA N
+constexpr int kStages = 4;
+constexpr uint32_t kABytes = 128 * 128;                   // 128 rows x 128 code bytes
+constexpr uint32_t kBBytes = 256 * 128;
+constexpr uint32_t kSfaBytes = 2 * 512, kSfbBytes = 4 * 512;
+constexpr uint32_t kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;  // 1024-multiple
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAccCol = 0;                           // accumulators: columns 0..255
+constexpr uint32_t kSfCol = 256;                          // per stage: 8 SFA + 16 SFB columns
+constexpr uint32_t kSfColsPerStage = 24;
+constexpr size_t kGemmSmem = 1024 + kStages * kStageBytes + 256;
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
   // K-major, 128-byte swizzle: 8-row atoms of 128-byte rows, SBO = 1024 B,
@@ -57,9 +64,9 @@ __device__ __forceinline__ uint64_t smem_desc_sf(const void* p) {
 }
 
 // Instruction descriptor of kind::mxf4 block_scale: E2M1 x E2M1, E8M0 scales,
-// K-major A and B, M = 128, N = kTileN; sf ids in bits 4-5 (B) and 29-30 (A).
+// K-major A and B, M = 128, N = 128; sf ids in bits 4-5 (B) and 29-30 (A).
 __host__ __device__ constexpr uint32_t gemm_idesc(uint32_t a_sf_id, uint32_t b_sf_id) {
-  return (b_sf_id << 4) | (1u << 7) | (1u << 10) | (uint32_t(kTileN >> 3) << 17) | (1u << 23) |
+  return (b_sf_id << 4) | (1u << 7) | (1u << 10) | (uint32_t(kHalfN >> 3) << 17) | (1u << 23) |
          (uint32_t(kTileM >> 4) << 24) | (a_sf_id << 29);
 }
 
@@ -112,29 +119,30 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-__global__ void __launch_bounds__(kGemmThreads) gemm_mxfp4_kernel(
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_mxfp4_kernel(
     const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
     const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, int64_t M, int64_t N,
     int64_t K, __nv_bfloat16* __restrict__ c, unsigned int* __restrict__ timeouts) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* sa = smem;                        // A tile, 16 KiB
-  uint8_t* sb = smem + kTileBytes;           // B tile, 16 KiB
-  uint8_t* ssfa = sb + kTileBytes;           // 2 scale atoms of A
-  uint8_t* ssfb = ssfa + kSfBytes;           // 2 scale atoms of B
-  uint64_t* bar_load = reinterpret_cast<uint64_t*>(ssfb + kSfBytes);
-  uint64_t* bar_mma = bar_load + 1;
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   int* failed = reinterpret_cast<int*>(tmem_base_slot + 1);
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int64_t m0 = (int64_t)blockIdx.y * kTileM, n0 = (int64_t)blockIdx.x * kTileN;
-  const int64_t ksteps = K / kTileK;
-  const int64_t sp4_a = K / 128, sp4_b = K / 128;  // scale atoms per 128-row block
+  const int ksteps = (int)(K / kTileK);
+  const int64_t sp4 = K / 128;  // scale atoms per 128-row block along K
 
   if (t == 0) {
-    mbar_init(bar_load, 1);
-    mbar_init(bar_mma, 1);
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
     fence_mbar_init();
     *failed = 0;
   }
@@ -147,72 +155,100 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_mxfp4_kernel(
   tc_fence_after();
   const uint32_t tmem = *tmem_base_slot;
 
-  if (t == 0) {
-    bool ok = true;
-    int load_pending = -1;  // parity of a load this thread stopped waiting for
-    for (int64_t ks = 0; ks < ksteps && ok; ++ks) {
-      const uint32_t ph = (uint32_t)(ks & 1);
-      // the previous step's MMAs have finished reading the tiles
-      if (ks > 0) ok = mbar_wait(bar_mma, ph ^ 1u);
-      if (!ok) break;
-      mbar_arrive_expect_tx(bar_load, 2 * kTileBytes + 2 * kSfBytes);
-      tma_load_2d(sa, &tmap_a, (int32_t)(ks * kTileK / 2), (int32_t)m0, bar_load);
-      tma_load_2d(sb, &tmap_b, (int32_t)(ks * kTileK / 2), (int32_t)n0, bar_load);
-      bulk_load_1d(ssfa, sfa + ((m0 / 128) * sp4_a + ks * 2) * 512, kSfBytes, bar_load);
-      bulk_load_1d(ssfb, sfb + ((n0 / 128) * sp4_b + ks * 2) * 512, kSfBytes, bar_load);
-      ok = mbar_wait(bar_load, ph);
-      if (!ok) {
-        load_pending = (int)ph;
-        break;
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int ks = 0; ks < ksteps; ++ks) {
+        const int s = ks % kStages;
+        if (ks >= kStages && !mbar_wait(&empty[s], (uint32_t)((ks / kStages - 1) & 1))) {
+          atomicExch(failed, 1);
+          break;
+        }
+        uint8_t* st = smem + s * kStageBytes;
+        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        const int32_t kx = ks * (kTileK / 2);
+        tma_load_2d(st, &tmap_a, kx, (int32_t)m0, &full[s]);
+        tma_load_2d(st + kABytes, &tmap_b, kx, (int32_t)n0, &full[s]);
+        tma_load_2d(st + kABytes + kABytes, &tmap_b, kx, (int32_t)(n0 + 128), &full[s]);
+        uint8_t* ssf = st + kABytes + kBBytes;
+        bulk_load_1d(ssf, sfa + ((m0 / 128) * sp4 + ks * 2) * 512, kSfaBytes, &full[s]);
+        bulk_load_1d(ssf + kSfaBytes, sfb + ((n0 / 128) * sp4 + ks * 2) * 512, kSfaBytes,
+                     &full[s]);
+        bulk_load_1d(ssf + kSfaBytes + kSfaBytes, sfb + ((n0 / 128 + 1) * sp4 + ks * 2) * 512,
+                     kSfaBytes, &full[s]);
+        issued = ks + 1;
       }
-      tc_fence_after();
-#pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        tc_copy_sf(tmem + kSfaCol + 4 * a, smem_desc_sf(ssfa + a * 512));
-        tc_copy_sf(tmem + kSfbCol + 4 * a, smem_desc_sf(ssfb + a * 512));
-      }
-      const uint64_t da = smem_desc_sw128(sa), db = smem_desc_sw128(sb);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        // K-half j covers elements 64j .. 64j+63 of the step: atom j/2, scale
-        // bytes 2(j%2) .. 2(j%2)+1 of each row's 32-bit scale column
-        const uint32_t sf_id = (uint32_t)(j & 1) * 2u;
-        const uint32_t tsfa = (tmem + kSfaCol + 4 * (j >> 1)) | (sf_id << 30);
-        const uint32_t tsfb = (tmem + kSfbCol + 4 * (j >> 1)) | (sf_id << 30);
-        tc_mma(tmem + kAccCol, da + (uint64_t)(2 * j), db + (uint64_t)(2 * j),
-               gemm_idesc(sf_id, sf_id), tsfa, tsfb, (ks > 0 || j > 0) ? 1u : 0u);
-      }
-      tc_commit(bar_mma);
+      // do not leave while copies of this CTA are still landing
+      for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
+        mbar_wait(&full[i % kStages], (uint32_t)((i / kStages) & 1));
     }
-    // the last commit: the accumulator is complete (or a wait gave up)
-    if (ok && ksteps > 0) ok = mbar_wait(bar_mma, (uint32_t)((ksteps - 1) & 1));
-    if (!ok) {
-      *failed = 1;
-      atomicAdd(timeouts, 1u);
-      // do not release the CTA while a requested copy may still land
-      if (load_pending >= 0) mbar_wait(bar_load, (uint32_t)load_pending);
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = true;
+      for (int ks = 0; ks < ksteps; ++ks) {
+        const int s = ks % kStages;
+        if (!mbar_wait(&full[s], (uint32_t)((ks / kStages) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint8_t* st = smem + s * kStageBytes;
+        const uint8_t* ssf = st + kABytes + kBBytes;
+        const uint32_t sfc = tmem + kSfCol + (uint32_t)(s * kSfColsPerStage);
+        // scale atoms -> TMEM: A atoms a = 0,1 at sfc + 4a; B (half h, atom a) at sfc + 8 + 8h + 4a
+#pragma unroll
+        for (int a = 0; a < 2; ++a) tc_copy_sf(sfc + 4 * a, smem_desc_sf(ssf + a * 512));
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int a = 0; a < 2; ++a)
+            tc_copy_sf(sfc + 8 + 8 * h + 4 * a, smem_desc_sf(ssf + kSfaBytes + (2 * h + a) * 512));
+        const uint64_t da = smem_desc_sw128(st);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          // K-half j = elements 64j .. 64j+63: atom j/2, scale bytes 2(j%2), 2(j%2)+1
+          const uint32_t sf_id = (uint32_t)(j & 1) * 2u;
+          const uint32_t tsfa = (sfc + 4 * (j >> 1)) | (sf_id << 30);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint64_t db = smem_desc_sw128(st + kABytes + h * kABytes);
+            const uint32_t tsfb = (sfc + 8 + 8 * h + 4 * (j >> 1)) | (sf_id << 30);
+            tc_mma(tmem + kAccCol + (uint32_t)(h * kHalfN), da + (uint64_t)(2 * j),
+                   db + (uint64_t)(2 * j), gemm_idesc(sf_id, sf_id), tsfa, tsfb,
+                   (ks > 0 || j > 0) ? 1u : 0u);
+          }
+        }
+        tc_commit(&empty[s]);  // the stage is free once these MMAs have run
+      }
+      if (!ok) atomicExch(failed, 1);
+      tc_commit(acc_full);  // every MMA issued so far has completed when this arrives
     }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-
-  if (!*failed) {
-    // epilogue: warp w reads lanes 32w .. 32w+31 (rows), 16 columns at a time
-    const int64_t row = m0 + warp * 32 + lane;
+  } else {
+    // ------------------------------------------------ epilogue warps 2..5
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may read
+    const bool ok = mbar_wait(acc_full, 0u);
+    tc_fence_after();
+    if (ok && !*((volatile int*)failed)) {
+      const int64_t row = m0 + quad * 32 + lane;
 #pragma unroll 1
-    for (int c0 = 0; c0 < kTileN; c0 += 16) {
-      uint32_t v[16];
-      tmem_ld16(tmem + kAccCol + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
-      tmem_ld_wait();
-      uint32_t o[8];
+      for (int c0 = 0; c0 < kTileN; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem + kAccCol + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
+        tmem_ld_wait();
+        uint32_t o[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = cvt_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-      if (row < M) {
-        uint8_t* dst = reinterpret_cast<uint8_t*>(c + row * N + n0 + c0);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
-        *reinterpret_cast<uint4*>(dst + 16) = make_uint4(o[4], o[5], o[6], o[7]);
+        for (int i = 0; i < 8; ++i)
+          o[i] = cvt_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+        if (row < M) {
+          uint8_t* dst = reinterpret_cast<uint8_t*>(c + row * N + n0 + c0);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(dst + 16) = make_uint4(o[4], o[5], o[6], o[7]);
+        }
       }
+    } else if (lane == 0 && quad == 0) {
+      atomicAdd(timeouts, 1u);
     }
   }
   tc_fence_before();
@@ -234,7 +270,7 @@ extern "C" mxb_status mxb_gemm_mxfp4(const void* a_codes, const void* a_scales_s
   MXB_REQUIRE(M >= 0 && N >= 0 && K >= 0 && M % kTileM == 0 && N % kTileN == 0 &&
                   K % kTileK == 0,
               MXB_ERR_INVALID_ARGUMENT,
-              "gemm_mxfp4: need M %% 128, N %% 128 and K %% 256 == 0 (M=%lld N=%lld K=%lld)",
+              "gemm_mxfp4: need M %% 128, N %% 256 and K %% 256 == 0 (M=%lld N=%lld K=%lld)",
               (long long)M, (long long)N, (long long)K);
   if (M == 0 || N == 0) return MXB_OK;
   MXB_REQUIRE(a_codes && a_scales_swizzled && b_codes && b_scales_swizzled && c,

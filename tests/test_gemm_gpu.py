@@ -31,7 +31,7 @@ def quantize(x, cuda):
     return q, s, swz
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 128, 256), (256, 384, 1024), (512, 256, 7168)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (256, 512, 1024), (512, 256, 7168), (384, 768, 2048)])
 def test_gemm_mxfp4(cuda, M, N, K):
     a = syn.config2(M, K, seed=41)
     b = syn.config2(N, K, seed=42)
