@@ -48,6 +48,14 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def measured_bf16_tflops():
+    """Dense BF16 tensor peak (burst) of this pool's B200s, else the recipe's fallback."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"])
+    return 1590.0
+
+
 class ClockSampler:
     """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
 
@@ -399,11 +407,12 @@ def time_other_ops(dev, stream, peak, only=None):
 
     sh = stream.cuda_stream
     res = {}
+    bf16_peak = measured_bf16_tflops()
 
     def want(*names):
         return only is None or only in names
 
-    def timeit(name, fn, alg_bytes, n=20):
+    def timeit(name, fn, alg_bytes, n=20, tflops=False):
         if not want(name):
             return
         if only is not None:
@@ -419,6 +428,10 @@ def time_other_ops(dev, stream, peak, only=None):
         torch.cuda.synchronize(dev)
         ms = a.elapsed_time(b) / n
         gbs = alg_bytes / (ms * 1e-3) / 1e9
+        if tflops:  # alg_bytes carries FLOP / 1000: gbs is then TFLOP/s
+            res[name] = {"us": round(ms * 1e3, 2), "tflops": round(gbs, 1),
+                         "frac_of_4x_bf16": round(gbs / (4 * bf16_peak), 4)}
+            return
         res[name] = {"us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
 
     C3 = ("dequant_bf16_config3", "mxfp4_to_fp8_rows_config3", "mxfp4_to_fp8_col_config3",
@@ -432,6 +445,8 @@ def time_other_ops(dev, stream, peak, only=None):
         _ops_config4(dev, sh, timeit, capi, syn)
     if want("moe_permute_wire_config5"):
         _ops_permute(dev, sh, timeit, capi, syn)
+    if want("gemm_mxfp4_8192x8192x7168"):
+        _ops_gemm(dev, sh, timeit, capi, syn)
     return res
 
 
@@ -525,6 +540,25 @@ def _ops_permute(dev, sh, timeit, capi, syn):
                              wire.data_ptr() + H // 2, 17 * H // 32, T, H, dst.data_ptr(), k,
                              oc.data_ptr(), os_.data_ptr(), T * k, sh),
            T * 17 * H // 32 + T * k * 17 * H // 32 + T * k * 4)
+
+
+def _ops_gemm(dev, sh, timeit, capi, syn):
+    import torch
+    # block-scaled MXFP4 GEMM (tcgen05) on quantizer-shaped operands: A [8192, 7168],
+    # B [8192, 7168] (codes + swizzled E8M0 scales), C bf16 [8192, 8192]; "gbs" here is
+    # TFLOP/s and "frac" is against 4x the measured dense BF16 peak (the FP4:BF16 ratio
+    # of the tensor cores), there being no measured FP4 peak
+    M, N, K = 8192, 8192, 7168
+    g = torch.Generator().manual_seed(9)
+    qa = torch.randint(0, 256, (M, K // 2), generator=g, dtype=torch.uint8).to(dev)
+    qb = torch.randint(0, 256, (N, K // 2), generator=g, dtype=torch.uint8).to(dev)
+    sa = torch.randint(120, 131, (M, K // 32), generator=g, dtype=torch.uint8).to(dev)
+    sb = torch.randint(120, 131, (N, K // 32), generator=g, dtype=torch.uint8).to(dev)
+    c = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    timeit("gemm_mxfp4_8192x8192x7168",
+           lambda: capi.call("mxb_gemm_mxfp4", qa.data_ptr(), sa.data_ptr(), qb.data_ptr(),
+                             sb.data_ptr(), M, N, K, c.data_ptr(), sh),
+           2 * M * N * K // 1000, tflops=True)
 
 
 def _ops_config4(dev, sh, timeit, capi, syn):
