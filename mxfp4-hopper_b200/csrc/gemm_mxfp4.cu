@@ -6,8 +6,8 @@
 // scales_row_swizzled (the tcgen05 block-scale layout: a 512-byte atom holds
 // the 4 scales of 128 rows, row r at (r % 32) * 16 + (r / 32) * 4).
 //
-// One CTA computes a 128 x 256 tile of C as two 128 x 128 accumulators in
-// tensor memory that share the A tile; the K loop walks 256-element steps
+// One CTA computes a 128 x 256 tile of C in one f32 accumulator in tensor
+// memory (128 lanes x 256 columns); the K loop walks 256-element steps
 // through a 4-stage shared-memory ring:
 //   * warp 0 (one thread) lands each step's A tile (128 rows x 128 bytes), B
 //     tile (256 rows x 128 bytes) with TMA (128-byte swizzle) and the step's
@@ -15,11 +15,12 @@
 //     completing on full[s];
 //   * warp 1 (one thread) copies the scale atoms into the stage's own tensor
 //     memory columns with tcgen05.cp (32 rows x 16 bytes replicated to the four
-//     lane quadrants: 4 columns per atom), issues 8 tcgen05.mma.kind::mxf4.
-//     block_scale.block32 per step (4 K-halves of 64 x 2 accumulators; the
-//     scale byte pair of a K-half is selected by the top two bits of the TMEM
-//     scale address) and commits them to empty[s], which frees the stage when
-//     they have run; after the last step it commits to acc_full;
+//     lane quadrants: 4 columns per atom; B's 128-row blocks of one K-atom sit
+//     in consecutive column groups), issues 4 tcgen05.mma.kind::mxf4.
+//     block_scale.block32 of 128 x 256 x 64 per step (the scale byte pair of a
+//     K-half is selected by the top two bits of the TMEM scale addresses) and
+//     commits them to empty[s], which frees the stage when they have run;
+//     after the last step it commits to acc_full;
 //   * warps 2..5 read the accumulators with tcgen05.ld (warp w owns lane
 //     quadrant w % 4 = rows 32(w%4) .. +31) and store BF16.
 // Descriptor formats follow the Blackwell UMMA descriptors (CUTLASS
@@ -36,7 +37,6 @@ namespace {
 
 constexpr int kGemmThreads = 192;                         // producer, MMA, 4 epilogue warps
 constexpr int kTileM = 128, kTileN = 256, kTileK = 256;   // elements
-constexpr int kHalfN = 128;                               // one accumulator / one MMA N
 constexpr int kStages = 4;
 constexpr uint32_t kABytes = 128 * 128;                   // 128 rows x 128 code bytes
 constexpr uint32_t kBBytes = 256 * 128;
@@ -64,9 +64,9 @@ __device__ __forceinline__ uint64_t smem_desc_sf(const void* p) {
 }
 
 // Instruction descriptor of kind::mxf4 block_scale: E2M1 x E2M1, E8M0 scales,
-// K-major A and B, M = 128, N = 128; sf ids in bits 4-5 (B) and 29-30 (A).
+// K-major A and B, M = 128, N = 256; sf ids in bits 4-5 (B) and 29-30 (A).
 __host__ __device__ constexpr uint32_t gemm_idesc(uint32_t a_sf_id, uint32_t b_sf_id) {
-  return (b_sf_id << 4) | (1u << 7) | (1u << 10) | (uint32_t(kHalfN >> 3) << 17) | (1u << 23) |
+  return (b_sf_id << 4) | (1u << 7) | (1u << 10) | (uint32_t(kTileN >> 3) << 17) | (1u << 23) |
          (uint32_t(kTileM >> 4) << 24) | (a_sf_id << 29);
 }
 
@@ -200,25 +200,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_mxfp4_kernel(
         // scale atoms -> TMEM: A atoms a = 0,1 at sfc + 4a; B (half h, atom a) at sfc + 8 + 8h + 4a
 #pragma unroll
         for (int a = 0; a < 2; ++a) tc_copy_sf(sfc + 4 * a, smem_desc_sf(ssf + a * 512));
+        // B atoms: 128-row block h of K-atom a at sfc + 8 + 8a + 4h (rows 128..255
+        // follow rows 0..127 in the next four columns)
 #pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
           for (int a = 0; a < 2; ++a)
-            tc_copy_sf(sfc + 8 + 8 * h + 4 * a, smem_desc_sf(ssf + kSfaBytes + (2 * h + a) * 512));
+            tc_copy_sf(sfc + 8 + 8 * a + 4 * h, smem_desc_sf(ssf + kSfaBytes + (2 * h + a) * 512));
         const uint64_t da = smem_desc_sw128(st);
+        const uint64_t db = smem_desc_sw128(st + kABytes);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           // K-half j = elements 64j .. 64j+63: atom j/2, scale bytes 2(j%2), 2(j%2)+1
           const uint32_t sf_id = (uint32_t)(j & 1) * 2u;
           const uint32_t tsfa = (sfc + 4 * (j >> 1)) | (sf_id << 30);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint64_t db = smem_desc_sw128(st + kABytes + h * kABytes);
-            const uint32_t tsfb = (sfc + 8 + 8 * h + 4 * (j >> 1)) | (sf_id << 30);
-            tc_mma(tmem + kAccCol + (uint32_t)(h * kHalfN), da + (uint64_t)(2 * j),
-                   db + (uint64_t)(2 * j), gemm_idesc(sf_id, sf_id), tsfa, tsfb,
-                   (ks > 0 || j > 0) ? 1u : 0u);
-          }
+          const uint32_t tsfb = (sfc + 8 + 8 * (j >> 1)) | (sf_id << 30);
+          tc_mma(tmem + kAccCol, da + (uint64_t)(2 * j), db + (uint64_t)(2 * j),
+                 gemm_idesc(sf_id, sf_id), tsfa, tsfb, (ks > 0 || j > 0) ? 1u : 0u);
         }
         tc_commit(&empty[s]);  // the stage is free once these MMAs have run
       }
