@@ -10,7 +10,10 @@ import torch
 
 import mxfp4_b200  # noqa: F401
 from omo import (omo_per_token_group_quant_fp4, omo_per_token_group_quant_fp4_fused_ToFp8,
-                 omo_quant_mxfp4_rowcol)
+                 omo_quant_mxfp4_rowcol, omo_swizzle_scales)
+from omo import omo_gemm_mxfp4 as _gemm_op
+from omo import omo_moe_permute_mxfp4 as _permute_op
+from omo import omo_swiglu_quant_mxfp4 as _swiglu_op
 
 fp8_type_ = torch.float8_e4m3fn
 uint8_type = torch.uint8
@@ -140,3 +143,47 @@ def omo_per_token_group_quant_mxfp4_fused_fp8(x: torch.Tensor):
         omo_per_token_group_quant_fp4_fused_ToFp8(x, x_q, x_s, y, y_s, 32, 1e-10, mxfp4_min,
                                                   mxfp4_max, False)
     return x_q, x_s, y, y_s
+
+
+def omo_swiglu_quant_mxfp4(x: torch.Tensor):
+    """Megatron's SwiGLU with fp4_input_store in one pass (megatron-0.15.0rc7.diff:164-193):
+    returns (silu(x[..., :H]) * x[..., H:] as BF16 [..., H], the rowwise MXFP4 of x: codes
+    [..., H] uint8 and E8M0 scales [rows, 2H/32] uint8)."""
+    assert x.is_contiguous() and x.shape[-1] % 64 == 0, "`x` must be contiguous with 2H % 64 == 0"
+    H = x.shape[-1] // 2
+    rows = x.numel() // x.shape[-1] if x.shape[-1] else 0
+    y = torch.empty((*x.shape[:-1], H), device=x.device, dtype=torch.bfloat16)
+    q = torch.empty((*x.shape[:-1], H), device=x.device, dtype=uint8_type)
+    s = torch.empty((rows, x.shape[-1] // 32), device=x.device, dtype=uint8_type)
+    if rows > 0:
+        _swiglu_op(x, y, q, s)
+    return y, q, s
+
+
+def omo_moe_permute_mxfp4(codes: torch.Tensor, scales: torch.Tensor, dst: torch.Tensor,
+                          num_out: int):
+    """MoE permute of MXFP4 rows (the MXFP4 branch of TE's moe_permute,
+    transformer_engine-2.8.diff:253-261,338-356): row i of codes [rows, H/2] and scales
+    [rows, H/32] goes to output rows dst[i, k] (int32 [rows, topk]; -1 = none) of the
+    returned (codes [num_out, H/2], scales [num_out, H/32])."""
+    oc = torch.empty((num_out, codes.shape[1]), device=codes.device, dtype=uint8_type)
+    os_ = torch.empty((num_out, scales.shape[1]), device=codes.device, dtype=uint8_type)
+    _permute_op(codes.contiguous(), scales.contiguous(), dst.to(torch.int32).contiguous(), oc, os_)
+    return oc, os_
+
+
+def omo_gemm_mxfp4(a_codes: torch.Tensor, a_scales: torch.Tensor, b_codes: torch.Tensor,
+                   b_scales: torch.Tensor) -> torch.Tensor:
+    """C = A . B^T in BF16 on the tcgen05 tensor cores from MXFP4 operands as the rowwise
+    quantizer returns them (codes [rows, K/2], E8M0 scales [rows, K/32]); the scales are
+    swizzled into the 128x4 block-scale layout here.  M % 128, N % 256, K % 256 == 0."""
+    M, N = a_codes.shape[0], b_codes.shape[0]
+    sa = torch.empty((align(M, 128), align(a_scales.shape[1], 4)), device=a_codes.device,
+                     dtype=uint8_type)
+    sb = torch.empty((align(N, 128), align(b_scales.shape[1], 4)), device=b_codes.device,
+                     dtype=uint8_type)
+    omo_swizzle_scales(a_scales.contiguous(), sa)
+    omo_swizzle_scales(b_scales.contiguous(), sb)
+    c = torch.empty((M, N), device=a_codes.device, dtype=torch.bfloat16)
+    _gemm_op(a_codes.contiguous(), sa, b_codes.contiguous(), sb, c)
+    return c

@@ -349,6 +349,79 @@ void omo_per_token_dequant_fp8(at::Tensor input_q, at::Tensor input_s, at::Tenso
                "omo_per_token_dequant_fp8");
 }
 
+// ---- operators with no reference binding: the next rows of the path
+void omo_swiglu_quant_mxfp4(at::Tensor input, at::Tensor output, at::Tensor codes,
+                            at::Tensor scales, double eps, double fp4_min, double fp4_max) {
+  OMO_CHECK_INPUT(input);
+  OMO_CHECK_INPUT(output);
+  OMO_CHECK_INPUT(codes);
+  OMO_CHECK_INPUT(scales);
+  check_dtype(input, at::kBFloat16, "input");
+  check_dtype(output, at::kBFloat16, "output");
+  check_dtype(codes, at::kByte, "codes");
+  check_dtype(scales, at::kByte, "scales");
+  if (input.numel() == 0) return;
+  const int64_t K = input.size(-1), M = input.numel() / K;
+  TORCH_CHECK(K % 64 == 0, "omo_swiglu_quant_mxfp4: the last dimension (2H) must be a multiple of 64");
+  TORCH_CHECK(output.numel() == M * K / 2 && codes.numel() == M * K / 2 &&
+                  scales.numel() == M * K / 32,
+              "omo_swiglu_quant_mxfp4: output [.., H], codes [.., H], scales [rows, 2H/32]");
+  c10::cuda::CUDAGuard g(input.device());
+  check_status(mxb_swiglu_quant_mxfp4(input.data_ptr(), M, K / 2, output.data_ptr(),
+                                      codes.data_ptr(), scales.data_ptr(), (float)eps,
+                                      (float)fp4_min, (float)fp4_max, cur_stream()),
+               "omo_swiglu_quant_mxfp4");
+}
+
+void omo_moe_permute_mxfp4(at::Tensor codes, at::Tensor scales, at::Tensor dst,
+                           at::Tensor out_codes, at::Tensor out_scales) {
+  OMO_CHECK_INPUT(codes);
+  OMO_CHECK_INPUT(scales);
+  OMO_CHECK_INPUT(dst);
+  OMO_CHECK_INPUT(out_codes);
+  OMO_CHECK_INPUT(out_scales);
+  check_dtype(codes, at::kByte, "codes");
+  check_dtype(scales, at::kByte, "scales");
+  check_dtype(dst, at::kInt, "dst");
+  TORCH_CHECK(codes.dim() == 2 && scales.dim() == 2 && dst.dim() == 2 &&
+                  codes.size(0) == scales.size(0) && dst.size(0) == codes.size(0),
+              "omo_moe_permute_mxfp4: codes [rows, H/2], scales [rows, H/32], dst [rows, topk]");
+  const int64_t rows = codes.size(0), H = codes.size(1) * 2;
+  TORCH_CHECK(scales.size(1) * 32 == H, "omo_moe_permute_mxfp4: scales must be [rows, H/32]");
+  TORCH_CHECK(out_codes.dim() == 2 && out_codes.size(1) == H / 2 && out_scales.dim() == 2 &&
+                  out_scales.size(1) == H / 32 && out_scales.size(0) == out_codes.size(0),
+              "omo_moe_permute_mxfp4: out_codes [n_out, H/2], out_scales [n_out, H/32]");
+  if (rows == 0) return;
+  c10::cuda::CUDAGuard g(codes.device());
+  check_status(mxb_moe_permute_mxfp4(codes.data_ptr(), H / 2, scales.data_ptr(), H / 32, rows, H,
+                                     (const int32_t*)dst.data_ptr(), (int)dst.size(1),
+                                     out_codes.data_ptr(), out_scales.data_ptr(),
+                                     out_codes.size(0), cur_stream()),
+               "omo_moe_permute_mxfp4");
+}
+
+void omo_gemm_mxfp4(at::Tensor a_codes, at::Tensor a_scales_swizzled, at::Tensor b_codes,
+                    at::Tensor b_scales_swizzled, at::Tensor c) {
+  OMO_CHECK_INPUT(a_codes);
+  OMO_CHECK_INPUT(a_scales_swizzled);
+  OMO_CHECK_INPUT(b_codes);
+  OMO_CHECK_INPUT(b_scales_swizzled);
+  OMO_CHECK_INPUT(c);
+  check_dtype(a_codes, at::kByte, "a_codes");
+  check_dtype(b_codes, at::kByte, "b_codes");
+  check_dtype(c, at::kBFloat16, "c");
+  TORCH_CHECK(a_codes.dim() == 2 && b_codes.dim() == 2 && a_codes.size(1) == b_codes.size(1),
+              "omo_gemm_mxfp4: a_codes [M, K/2] and b_codes [N, K/2]");
+  const int64_t M = a_codes.size(0), N = b_codes.size(0), K = a_codes.size(1) * 2;
+  TORCH_CHECK(c.numel() == M * N, "omo_gemm_mxfp4: c must be [M, N]");
+  TORCH_CHECK(a_scales_swizzled.numel() == M * K / 32 && b_scales_swizzled.numel() == N * K / 32,
+              "omo_gemm_mxfp4: swizzled scales must hold rows * K/32 bytes");
+  c10::cuda::CUDAGuard g(a_codes.device());
+  check_status(mxb_gemm_mxfp4(a_codes.data_ptr(), a_scales_swizzled.data_ptr(), b_codes.data_ptr(),
+                              b_scales_swizzled.data_ptr(), M, N, K, c.data_ptr(), cur_stream()),
+               "omo_gemm_mxfp4");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(omo, m) {
@@ -397,4 +470,14 @@ PYBIND11_MODULE(omo, m) {
         py::arg("input"), py::arg("output_q"), py::arg("output_s"), py::arg("eps") = 1e-10);
   m.def("omo_per_token_dequant_fp8", &omo_per_token_dequant_fp8, "Per-token FP8 dequantization",
         py::arg("input_q"), py::arg("input_s"), py::arg("output"));
+  m.def("omo_swiglu_quant_mxfp4", &omo_swiglu_quant_mxfp4,
+        "SwiGLU of [.., 2H] and the rowwise MXFP4 of its input, one pass", py::arg("input"),
+        py::arg("output"), py::arg("codes"), py::arg("scales"), py::arg("eps") = 1e-10,
+        py::arg("fp4_min") = -6.0, py::arg("fp4_max") = 6.0);
+  m.def("omo_moe_permute_mxfp4", &omo_moe_permute_mxfp4,
+        "MoE permute of MXFP4 rows (codes and scales) to expert slots", py::arg("codes"),
+        py::arg("scales"), py::arg("dst"), py::arg("out_codes"), py::arg("out_scales"));
+  m.def("omo_gemm_mxfp4", &omo_gemm_mxfp4, "Block-scaled MXFP4 GEMM C = A . B^T (tcgen05)",
+        py::arg("a_codes"), py::arg("a_scales_swizzled"), py::arg("b_codes"),
+        py::arg("b_scales_swizzled"), py::arg("c"));
 }

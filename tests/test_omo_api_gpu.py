@@ -152,3 +152,42 @@ def test_wrapper_rejects_non_contiguous(cuda, api):
     c, s = _codes(64, 128, seed=29)
     with pytest.raises(AssertionError):
         dq.omo_per_token_mxfp4ToBf16_dequant_wrapper(c.to(cuda).t(), s.to(cuda), torch.bfloat16)
+
+
+# ------------------------------------------------------------------ next rows of the path
+def test_swiglu_quant_wrapper(cuda, orc, api):
+    _, mx, _ = api
+    x = syn.config1(96, 1024, seed=51)
+    y, q, s = mx.omo_swiglu_quant_mxfp4(x.to(cuda))
+    rq, rs = orc.quant_rows(H.np_u16(x))
+    H.assert_bytes_equal(H.np_u8(q), rq, "codes")
+    H.assert_bytes_equal(H.np_u8(s), rs, "scales")
+    xf = x.float()
+    ref = (torch.nn.functional.silu(xf[:, :512]) * xf[:, 512:]).to(torch.bfloat16)
+    assert np.abs(H.np_u16(y).astype(np.int32) - H.np_u16(ref).astype(np.int32)).max() <= 1
+
+
+def test_moe_permute_wrapper(cuda, api):
+    _, mx, _ = api
+    g = np.random.default_rng(52)
+    rows, Hd, topk = 64, 1024, 4
+    codes = torch.from_numpy(g.integers(0, 256, (rows, Hd // 2), dtype=np.uint8)).to(cuda)
+    scales = torch.from_numpy(g.integers(100, 150, (rows, Hd // 32), dtype=np.uint8)).to(cuda)
+    dst = torch.from_numpy(g.permutation(rows * topk).astype(np.int32).reshape(rows, topk)).to(cuda)
+    oc, os_ = mx.omo_moe_permute_mxfp4(codes, scales, dst, rows * topk)
+    inv = torch.empty(rows * topk, dtype=torch.long, device=cuda)
+    inv[dst.reshape(-1).long()] = torch.arange(rows, device=cuda).repeat_interleave(topk)
+    assert torch.equal(oc, codes[inv]) and torch.equal(os_, scales[inv])
+
+
+def test_gemm_wrapper(cuda, api):
+    _, mx, _ = api
+    from test_gemm_gpu import dequant_np
+    a = syn.config2(256, 512, seed=53)
+    b = syn.config2(256, 512, seed=54)
+    qa, sa = mx.omo_per_token_group_quant_mxfp4(a.to(cuda))
+    qb, sb = mx.omo_per_token_group_quant_mxfp4(b.to(cuda))
+    c = mx.omo_gemm_mxfp4(qa, sa, qb, sb)
+    ref = dequant_np(H.np_u8(qa), H.np_u8(sa)) @ dequant_np(H.np_u8(qb), H.np_u8(sb)).T
+    scale = np.maximum(np.abs(ref).max(axis=1, keepdims=True), 1e-30)
+    assert (np.abs(c.float().cpu().numpy() - ref) / scale).max() < 2 ** -7
