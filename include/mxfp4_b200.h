@@ -287,7 +287,9 @@ mxb_status mxb_moe_permute_mxfp4(const void* codes, int64_t codes_pitch, const v
  * The same semantics as DeepEP's intranode dispatch/combine with the MXFP4
  * payload of the reference (deep_ep-1.2.1.diff:455-549, megatron-0.15.0rc7.diff:
  * 290-311), without host synchronisation.  Parity alternates per step.  All
- * cross-GPU waits are bounded; mxb_ep_wait_timeouts() counts waits that gave up. */
+ * cross-GPU waits are bounded; mxb_ep_wait_timeouts() counts waits that gave up.
+ * Layout limits: world <= 32, topk <= 32, world * topk <= 256, hidden a multiple
+ * of 512 and at most 65536. */
 typedef struct {
   int64_t sig_off, cnt_off, wire_off, meta_off, back_off; /* byte offsets in the buffer */
   int64_t tcap;                                           /* max tokens per rank */

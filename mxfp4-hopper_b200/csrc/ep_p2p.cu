@@ -33,6 +33,7 @@ namespace {
 static __device__ unsigned int g_ep_timeouts;
 constexpr uint32_t kPeerSpins = 1u << 22;  // polls of ~64 ns sleep each
 constexpr int kP2PThreads = 256;
+constexpr int kMaxScaleBytes = 2048;  // H / 32 for H <= 65536
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -158,33 +159,53 @@ __global__ void __launch_bounds__(kP2PThreads) ep_dispatch_p2p_kernel(
     const int64_t* __restrict__ topk_idx, const float* __restrict__ topk_w,
     const uint64_t* __restrict__ bases, mxb_ep_layout L, int parity) {
   __shared__ int64_t dst_row[64];
+  __shared__ __align__(16) uint8_t scale_bytes[kMaxScaleBytes];
   const int G = L.world, H = L.hidden;
   const int64_t nb = H / 32, rb = H / 2 + H / 32;
   const int32_t* cnt = cnt_of(bases, L, parity);
+  int64_t off = 0;  // thread g < G: rows that lower ranks send to g come first
+  if (threadIdx.x < G)
+    for (int s = 0; s < L.rank; ++s) off += cnt[s * G + threadIdx.x];
+  const int64_t b0 = threadIdx.x;
   for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const uint8_t* xr = x + t * H * 2;
+    uint4 a[4];
+    if (b0 < nb) {  // the first block's loads go out before the barrier
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = ld_stream_v4(xr + b0 * 64 + i * 16);
+    }
     if (threadIdx.x < G) {
-      const int g = threadIdx.x;
-      const int32_t wi = within[t * G + g];
-      int64_t off = 0;
-      for (int s = 0; s < L.rank; ++s) off += cnt[s * G + g];  // rows from lower ranks first
-      dst_row[g] = wi < 0 ? -1 : off + wi;
+      const int32_t wi = within[t * G + threadIdx.x];
+      dst_row[threadIdx.x] = wi < 0 ? -1 : off + wi;
     }
     __syncthreads();
-    const uint8_t* xr = x + t * H * 2;
-    for (int64_t b = threadIdx.x; b < nb; b += kP2PThreads) {
-      const uint4 a0 = ld_stream_v4(xr + b * 64), a1 = ld_stream_v4(xr + b * 64 + 16);
-      const uint4 a2 = ld_stream_v4(xr + b * 64 + 32), a3 = ld_stream_v4(xr + b * 64 + 48);
-      const uint32_t w[16] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w,
-                              a2.x, a2.y, a2.z, a2.w, a3.x, a3.y, a3.z, a3.w};
+    for (int64_t b = b0; b < nb; b += kP2PThreads) {
+      if (b != b0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = ld_stream_v4(xr + b * 64 + i * 16);
+      }
+      const uint32_t w[16] = {a[0].x, a[0].y, a[0].z, a[0].w, a[1].x, a[1].y, a[1].z, a[1].w,
+                              a[2].x, a[2].y, a[2].z, a[2].w, a[3].x, a[3].y, a[3].z, a[3].w};
       uint32_t out[4], byte;
       p2p_quant_block(w, out, byte);
+      scale_bytes[b] = (uint8_t)byte;
       for (int g = 0; g < G; ++g) {
         const int64_t r = dst_row[g];
         if (r < 0) continue;
         uint8_t* row = peer(bases, g) + L.wire_off + r * rb;
         *reinterpret_cast<uint4*>(row + b * 16) = make_uint4(out[0], out[1], out[2], out[3]);
-        row[H / 2 + b] = (uint8_t)byte;
       }
+    }
+    __syncthreads();
+    // the row's scale bytes go out as 16-byte stores (H / 32 is a multiple of 16)
+    const int nv = (int)(nb / 16);
+    for (int i = threadIdx.x; i < G * nv; i += kP2PThreads) {
+      const int g = i / nv, q = i - g * nv;
+      const int64_t r = dst_row[g];
+      if (r < 0) continue;
+      uint8_t* row = peer(bases, g) + L.wire_off + r * rb;
+      *reinterpret_cast<uint4*>(row + H / 2 + q * 16) =
+          *reinterpret_cast<const uint4*>(scale_bytes + q * 16);
     }
     // routing metadata: expert id local to the destination (or -1), weight (or 0)
     for (int i = threadIdx.x; i < G * L.topk; i += kP2PThreads) {
@@ -222,31 +243,61 @@ __global__ void __launch_bounds__(kP2PThreads) ep_return_p2p_kernel(
     back_off[s] = o;
   }
   __syncthreads();
-  int64_t R = 0;
-  for (int s = 0; s < G; ++s) R += col[s];
+  // Rows are visited source-minor (i -> j = i / G, s = i % G) so that at any
+  // moment the CTAs write to every source, local HBM and NVLink together.
+  int64_t cmax = 0;
+  for (int s = 0; s < G; ++s) cmax = max(cmax, (int64_t)col[s]);
   const uint8_t* wire = peer(bases, L.rank) + L.wire_off;
   const int32_t* meta = reinterpret_cast<const int32_t*>(peer(bases, L.rank) + L.meta_off);
   const int64_t chunks = H / 8;
-  for (int64_t r = blockIdx.x; r < R; r += gridDim.x) {
-    int s = 0;
+  for (int64_t i = blockIdx.x; i < cmax * G; i += gridDim.x) {
+    const int s = (int)(i % G);
+    const int64_t j = i / G;
+    if (j >= col[s]) continue;
     int64_t start = 0;
-    while (s < G - 1 && r >= start + col[s]) start += col[s++];
-    const int64_t dst = back_off[s] + (r - start);
+    for (int q = 0; q < s; ++q) start += col[q];
+    const int64_t r = start + j;
+    const int64_t dst = back_off[s] + j;
     uint8_t* out = peer(bases, s) + L.back_off + dst * H * 2;
     float wsum = 0.0f;
-    if (!y_in) {
+    if (!y_in) {  // lane j loads weight j; the sum keeps the order j = 0, 1, ...
       const int32_t* m = meta + r * 2 * L.topk;
-      wsum = __int_as_float(m[L.topk]);
-      for (int j = 1; j < L.topk; ++j) wsum += __int_as_float(m[L.topk + j]);
+      const int lane = threadIdx.x & 31;
+      const float wj = lane < L.topk ? __int_as_float(m[L.topk + lane]) : 0.0f;
+      wsum = __shfl_sync(0xffffffffu, wj, 0);
+      for (int j = 1; j < L.topk; ++j) wsum += __shfl_sync(0xffffffffu, wj, j);
     }
     const uint8_t* row = wire + r * rb;
-    for (int64_t c = threadIdx.x; c < chunks; c += kP2PThreads) {
-      uint4 v;
+    constexpr int kU = 4;  // chunks per thread with their loads issued together
+    for (int64_t c0 = threadIdx.x; c0 < chunks; c0 += kP2PThreads * kU) {
       if (y_in) {
-        v = *reinterpret_cast<const uint4*>(y_in + (r * H + c * 8) * 2);
-      } else {
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(row + c * 4);
-        const uint32_t e = row[H / 2 + (c >> 2)];
+        uint4 v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int64_t c = c0 + u * kP2PThreads;
+          if (c < chunks) v[u] = *reinterpret_cast<const uint4*>(y_in + (r * H + c * 8) * 2);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int64_t c = c0 + u * kP2PThreads;
+          if (c < chunks) *reinterpret_cast<uint4*>(out + c * 16) = v[u];
+        }
+        continue;
+      }
+      uint32_t wv[kU], ev[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t c = c0 + u * kP2PThreads;
+        if (c < chunks) {
+          wv[u] = *reinterpret_cast<const uint32_t*>(row + c * 4);
+          ev[u] = row[H / 2 + (c >> 2)];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t c = c0 + u * kP2PThreads;
+        if (c >= chunks) continue;
+        const uint32_t w = wv[u], e = ev[u];
         uint32_t o[4];
         e2m1x4_to_bf16x4(w, o[0], o[1]);
         e2m1x4_to_bf16x4(w >> 16, o[2], o[3]);
@@ -263,91 +314,210 @@ __global__ void __launch_bounds__(kP2PThreads) ep_return_p2p_kernel(
 #pragma unroll
         for (int i = 0; i < 4; ++i)
           o[i] = cvt_bf16x2(bf16lo_to_f(o[i]) * wsum, bf16hi_to_f(o[i]) * wsum);
-        v = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(out + c * 16) = make_uint4(o[0], o[1], o[2], o[3]);
       }
-      *reinterpret_cast<uint4*>(out + c * 16) = v;
     }
   }
   __threadfence_system();
 }
 
-// Routing without host synchronisation.  CTA g scans the tokens in order and
-// gives every token routed to rank g its index among them (within[t, g], -1 if
-// the token does not go to g); send_counts[g] is the number of such tokens.
-constexpr int kRouteThreads = 1024;
+// Destination rank of expert id e, or -1 when e / experts_per_rank (C
+// division) lies outside [0, G).
+__device__ __forceinline__ int route_rank(int64_t e, int experts_per_rank, int G) {
+  const int64_t q = (e >= 0 && e <= 0x7FFFFFFFLL)
+                        ? (int64_t)((uint32_t)e / (uint32_t)experts_per_rank)
+                        : e / experts_per_rank;
+  return q >= 0 && q < G ? (int)q : -1;
+}
 
-__global__ void __launch_bounds__(kRouteThreads) ep_route_kernel(
+// Mask of the destination ranks of token t (bit g set if any of its k experts
+// lives on rank g), with 8 id loads in flight.
+__device__ __forceinline__ uint64_t route_mask(const int64_t* __restrict__ topk_idx, int64_t t,
+                                               int k, int experts_per_rank, int G) {
+  const int64_t* p = topk_idx + t * k;
+  uint64_t mask = 0;
+  for (int j0 = 0; j0 < k; j0 += 8) {
+    int64_t e[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) e[u] = j0 + u < k ? p[j0 + u] : -1;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int q = j0 + u < k ? route_rank(e[u], experts_per_rank, G) : -1;
+      if (q >= 0) mask |= 1ull << q;
+    }
+  }
+  return mask;
+}
+
+// Routing without host synchronisation, in two launches over tiles of
+// kRouteTile tokens (one token per thread).
+//   ep_route_tile_kernel: within[t, g] = token t's index among the tokens of
+//     its tile routed to rank g (ballot per rank, then a scan over the tile's
+//     warps), -1 if t does not go to g.  The tile's last token carries the
+//     tile's count c for every rank it does not go to, as -(c + 2), so the
+//     count of every tile can be read back from that one row (c = w + 1 for
+//     w >= 0, -w - 2 otherwise).
+//   ep_route_prefix_kernel (one CTA): reads every tile's counts, turns them
+//     into per-rank prefixes, adds each tile's prefix to its entries, restores
+//     -1 and writes send_counts[g] = number of tokens routed to g.  T * G
+//     entries are small next to the expert ids the first launch reads.
+// The result: within[t, g] is t's index among all tokens routed to g, in
+// token order.
+constexpr int kRouteTile = 256;
+constexpr int kRouteThreads = 1024;
+constexpr int kRouteMaxEntries = 16384;  // tiles * G held in shared memory (64 KB)
+
+__global__ void __launch_bounds__(kRouteTile) ep_route_tile_kernel(
+    const int64_t* __restrict__ topk_idx, int64_t T, int k, int experts_per_rank, int G,
+    int32_t* __restrict__ within) {
+  __shared__ int32_t warp_base[kRouteTile / 32][64];
+  const int t0 = threadIdx.x, lane = t0 & 31, warp = t0 >> 5;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  const int64_t base = (int64_t)blockIdx.x * kRouteTile, t = base + t0;
+  const int64_t last = min(T, base + kRouteTile) - 1;
+  const uint64_t mask = t < T ? route_mask(topk_idx, t, k, experts_per_rank, G) : 0;
+  for (int g = 0; g < G; ++g) {
+    const uint32_t b = __ballot_sync(0xffffffffu, (mask >> g) & 1);
+    if (lane == 0) warp_base[warp][g] = __popc(b);
+  }
+  __syncthreads();
+  if (t0 < G) {  // exclusive scan over the warps, per rank
+    int32_t acc = 0;
+    for (int w = 0; w < kRouteTile / 32; ++w) {
+      const int32_t v = warp_base[w][t0];
+      warp_base[w][t0] = acc;
+      acc += v;
+    }
+  }
+  __syncthreads();
+  for (int g = 0; g < G; ++g) {
+    const uint32_t b = __ballot_sync(0xffffffffu, (mask >> g) & 1);
+    if (t > last) continue;
+    const bool hit = (mask >> g) & 1;
+    const int32_t idx = warp_base[warp][g] + __popc(b & lt_mask);
+    // for the last token, idx + hit is the tile's count for g
+    within[t * G + g] = hit ? idx : (t == last ? -(idx + 2) : -1);
+  }
+}
+
+__global__ void __launch_bounds__(kRouteThreads) ep_route_prefix_kernel(
+    int64_t T, int G, int tiles, int32_t* __restrict__ within, int32_t* __restrict__ send_counts) {
+  extern __shared__ int32_t pref[];  // [tiles][G]: counts, then exclusive prefixes
+  for (int i = threadIdx.x; i < tiles * G; i += kRouteThreads) {
+    const int q = i / G, g = i - q * G;
+    const int64_t last = min(T, (int64_t)(q + 1) * kRouteTile) - 1;
+    const int32_t w = within[last * G + g];
+    pref[i] = w >= 0 ? w + 1 : -w - 2;
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    int32_t acc = 0;
+    for (int q = 0; q < tiles; ++q) {
+      const int32_t c = pref[q * G + g];
+      pref[q * G + g] = acc;
+      acc += c;
+    }
+    send_counts[g] = acc;
+  }
+  __syncthreads();
+  const uint32_t n = (uint32_t)(T * G), row_elems = (uint32_t)(kRouteTile * G);
+  for (uint32_t i = threadIdx.x; i < n; i += kRouteThreads) {
+    const uint32_t q = i / row_elems, g = i % (uint32_t)G;
+    const int32_t w = within[i];
+    within[i] = w >= 0 ? w + pref[q * G + g] : -1;
+  }
+}
+
+// Fallback for more than kRouteMaxEntries tile counts: one CTA walks the
+// tokens in order with a running per-rank count.
+
+__global__ void __launch_bounds__(kRouteThreads) ep_route_serial_kernel(
     const int64_t* __restrict__ topk_idx, int64_t T, int k, int experts_per_rank, int G,
     int32_t* __restrict__ within, int32_t* __restrict__ send_counts) {
-  __shared__ int32_t warp_sums[kRouteThreads / 32];
-  const int g = blockIdx.x, t0 = threadIdx.x, lane = t0 & 31, warp = t0 >> 5;
-  const int64_t per = (T + kRouteThreads - 1) / kRouteThreads;  // tokens per thread
-  const int64_t lo = t0 * per, hi = min(T, lo + per);
-  auto hits = [&](int64_t t) {
-    bool h = false;
-    for (int j = 0; j < k; ++j) h |= (topk_idx[t * k + j] / experts_per_rank) == g;
-    return h;
-  };
-  int32_t c = 0;
-  for (int64_t t = lo; t < hi; ++t) c += hits(t) ? 1 : 0;
-  // block-wide exclusive scan of c
-  int32_t v = c;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int32_t n = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v += n;
-  }
-  if (lane == 31) warp_sums[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    int32_t ws = warp_sums[lane];
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int32_t n = __shfl_up_sync(0xffffffffu, ws, o);
-      if (lane >= o) ws += n;
+  __shared__ int32_t warp_base[kRouteThreads / 32][64];
+  __shared__ int32_t run[64];
+  const int t0 = threadIdx.x, lane = t0 & 31, warp = t0 >> 5;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  if (t0 < G) run[t0] = 0;
+  for (int64_t base = 0; base < T; base += kRouteThreads) {
+    const int64_t t = base + t0;
+    const uint64_t mask = t < T ? route_mask(topk_idx, t, k, experts_per_rank, G) : 0;
+    for (int g = 0; g < G; ++g) {
+      const uint32_t b = __ballot_sync(0xffffffffu, (mask >> g) & 1);
+      if (lane == 0) warp_base[warp][g] = __popc(b);
     }
-    warp_sums[lane] = ws;  // inclusive over warps
+    __syncthreads();
+    if (t0 < G) {
+      int32_t acc = run[t0];
+      for (int w = 0; w < kRouteThreads / 32; ++w) {
+        const int32_t v = warp_base[w][t0];
+        warp_base[w][t0] = acc;
+        acc += v;
+      }
+      run[t0] = acc;
+    }
+    __syncthreads();
+    for (int g = 0; g < G; ++g) {
+      const uint32_t b = __ballot_sync(0xffffffffu, (mask >> g) & 1);
+      if (t < T)
+        within[t * G + g] = ((mask >> g) & 1) ? warp_base[warp][g] + __popc(b & lt_mask) : -1;
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  int32_t base = v - c + (warp > 0 ? warp_sums[warp - 1] : 0);
-  for (int64_t t = lo; t < hi; ++t) within[t * G + g] = hits(t) ? base++ : -1;
-  if (t0 == kRouteThreads - 1) send_counts[g] = warp_sums[31];
+  if (t0 < G) send_counts[t0] = run[t0];
 }
 
 // Local combine of the rows returned to this rank: out[t] = bf16(sum over g of
 // float(back[slot(t, g)])), slot(t, g) = sum_{g' < g} send_counts[g'] + within[t, g].
+// Work items are (token, 8-element chunk) pairs over a grid-stride loop with
+// no barrier inside; the slot offsets sit in shared memory and the loads of up
+// to 4 sources are issued before their sums.
 __global__ void __launch_bounds__(kP2PThreads) ep_p2p_combine_kernel(
     const uint8_t* __restrict__ back, int64_t T, int64_t H, const int32_t* __restrict__ within,
     const int32_t* __restrict__ send_counts, int G, uint8_t* __restrict__ out) {
-  __shared__ int64_t src[64];
-  const int64_t chunks = H / 8;
-  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
-    if (threadIdx.x < G) {
-      const int g = threadIdx.x;
-      int64_t off = 0;
-      for (int q = 0; q < g; ++q) off += send_counts[q];
-      const int32_t wi = within[t * G + g];
-      src[g] = wi < 0 ? -1 : off + wi;
+  __shared__ int64_t off[64];
+  if (threadIdx.x == 0) {
+    int64_t o = 0;
+    for (int g = 0; g < G; ++g) {
+      off[g] = o;
+      o += send_counts[g];
     }
-    __syncthreads();
-    for (int64_t c = threadIdx.x; c < chunks; c += kP2PThreads) {
-      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int g = 0; g < G; ++g) {
-        const int64_t sl = src[g];
-        if (sl < 0) continue;
-        const uint4 v = *reinterpret_cast<const uint4*>(back + (sl * H + c * 8) * 2);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  }
+  __syncthreads();
+  const int64_t chunks = H / 8, n = T * chunks;
+  const bool small = n <= 0x7FFFFFFFLL;
+  for (int64_t i = (int64_t)blockIdx.x * kP2PThreads + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * kP2PThreads) {
+    const int64_t t = small ? (int64_t)((uint32_t)i / (uint32_t)chunks) : i / chunks;
+    const int64_t c = i - t * chunks;
+    const int32_t* wt = within + t * G;
+    // A source that sent nothing adds +0, which leaves the sum unchanged: it
+    // starts at +0 and so is never -0.
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int g0 = 0; g0 < G; g0 += 4) {
+      int32_t wi[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          acc[2 * i] += bf16lo_to_f(w[i]);
-          acc[2 * i + 1] += bf16hi_to_f(w[i]);
+      for (int u = 0; u < 4; ++u) wi[u] = g0 + u < G ? wt[g0 + u] : -1;
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        v[u] = wi[u] < 0 ? make_uint4(0, 0, 0, 0)
+                         : *reinterpret_cast<const uint4*>(
+                               back + ((off[g0 + u] + wi[u]) * H + c * 8) * 2);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[2 * q] += bf16lo_to_f(w[q]);
+          acc[2 * q + 1] += bf16hi_to_f(w[q]);
         }
       }
-      *reinterpret_cast<uint4*>(out + (t * H + c * 8) * 2) =
-          make_uint4(cvt_bf16x2(acc[0], acc[1]), cvt_bf16x2(acc[2], acc[3]),
-                     cvt_bf16x2(acc[4], acc[5]), cvt_bf16x2(acc[6], acc[7]));
     }
-    __syncthreads();
+    *reinterpret_cast<uint4*>(out + (t * H + c * 8) * 2) =
+        make_uint4(cvt_bf16x2(acc[0], acc[1]), cvt_bf16x2(acc[2], acc[3]),
+                   cvt_bf16x2(acc[4], acc[5]), cvt_bf16x2(acc[6], acc[7]));
   }
 }
 
@@ -373,7 +543,8 @@ int p2p_grid(int64_t rows) {
 mxb_status check_layout(const mxb_ep_layout* L, const char* what) {
   MXB_REQUIRE(L && L->world >= 1 && L->world <= 32 && L->rank >= 0 && L->rank < L->world &&
                   L->topk >= 1 && L->topk <= 32 && L->world * L->topk <= 256 &&
-                  L->hidden % 512 == 0 && L->hidden > 0 && L->experts_per_rank >= 1,
+                  L->hidden % 512 == 0 && L->hidden > 0 && L->hidden <= 32 * kMaxScaleBytes &&
+                  L->experts_per_rank >= 1,
               MXB_ERR_INVALID_ARGUMENT, "%s: invalid layout", what);
   return MXB_OK;
 }
@@ -495,13 +666,33 @@ extern "C" mxb_status mxb_ep_p2p_return(const void* y, const uint64_t* bases,
 extern "C" mxb_status mxb_ep_route(const int64_t* topk_idx, int64_t T, int32_t topk,
                                    int32_t experts_per_rank, int32_t world, int32_t* within,
                                    int32_t* send_counts, mxb_stream_t stream) {
-  MXB_REQUIRE(T >= 0 && topk >= 1 && experts_per_rank >= 1 && world >= 1 && world <= 64,
+  MXB_REQUIRE(T >= 0 && topk >= 1 && topk <= 1024 && experts_per_rank >= 1 && world >= 1 &&
+                  world <= 64,
               MXB_ERR_INVALID_ARGUMENT, "ep_route: bad arguments");
   MXB_REQUIRE(topk_idx && within && send_counts, MXB_ERR_INVALID_ARGUMENT,
               "ep_route: null pointer");
-  ep_route_kernel<<<world, kRouteThreads, 0, to_cuda(stream)>>>(topk_idx, T, topk,
-                                                                experts_per_rank, world, within,
-                                                                send_counts);
+  if (T == 0) {
+    const cudaError_t e = cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * world, to_cuda(stream));
+    MXB_REQUIRE(e == cudaSuccess, MXB_ERR_CUDA, "ep_route: memset failed: %s",
+                cudaGetErrorString(e));
+    return MXB_OK;
+  }
+  const int64_t tiles = (T + kRouteTile - 1) / kRouteTile;
+  if (tiles * world > kRouteMaxEntries || T * world > 0x7FFFFFFFLL) {
+    ep_route_serial_kernel<<<1, kRouteThreads, 0, to_cuda(stream)>>>(
+        topk_idx, T, topk, experts_per_rank, world, within, send_counts);
+  } else {
+    ep_route_tile_kernel<<<(int)tiles, kRouteTile, 0, to_cuda(stream)>>>(
+        topk_idx, T, topk, experts_per_rank, world, within);
+    const size_t smem = sizeof(int32_t) * tiles * world;
+    if (smem > 48 * 1024) {
+      const cudaError_t e = cudaFuncSetAttribute(
+          ep_route_prefix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      MXB_REQUIRE(e == cudaSuccess, MXB_ERR_CUDA, "ep_route: %s", cudaGetErrorString(e));
+    }
+    ep_route_prefix_kernel<<<1, kRouteThreads, smem, to_cuda(stream)>>>(T, world, (int)tiles,
+                                                                        within, send_counts);
+  }
   return launch_status("ep_route");
 }
 

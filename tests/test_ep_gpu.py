@@ -42,7 +42,8 @@ def test_pack_unpack_combine_kernels(cuda, world, T, H):
                           combine_rows(y_ref, r.slots.numpy()))
 
 
-@pytest.mark.parametrize("world,T", [(1, 5), (2, 4096), (8, 4096), (8, 3000)])
+@pytest.mark.parametrize("world,T", [(1, 5), (2, 1), (2, 4096), (8, 4096), (8, 3000), (64, 2500),
+                                     (64, 51200), (64, 65792)])
 def test_route_kernel(cuda, world, T):
     from mxfp4_b200 import capi
     from mxfp4_b200.ep import local_route
@@ -53,6 +54,22 @@ def test_route_kernel(cuda, world, T):
     capi.call("mxb_ep_route", idx.data_ptr(), T, 8, 256 // world, world, within.data_ptr(),
               counts.data_ptr(), torch.cuda.current_stream().cuda_stream)
     w_ref, c_ref, _ = local_route(idx, world, 256)
+    assert torch.equal(within, w_ref) and torch.equal(counts, c_ref)
+
+
+@pytest.mark.parametrize("world,T,topk,experts", [(4, 2100, 3, 64), (3, 1025, 1, 9),
+                                                  (16, 700, 13, 160)])
+def test_route_kernel_odd_topk(cuda, world, T, topk, experts):
+    """Top-k widths that do not divide the tile, repeated experts of one rank."""
+    from mxfp4_b200 import capi
+    from mxfp4_b200.ep import local_route
+    g = torch.Generator().manual_seed(world * 1000 + topk)
+    idx = torch.randint(0, experts, (T, topk), generator=g, dtype=torch.int64).to(cuda)
+    within = torch.empty(T, world, dtype=torch.int32, device=cuda)
+    counts = torch.empty(world, dtype=torch.int32, device=cuda)
+    capi.call("mxb_ep_route", idx.data_ptr(), T, topk, experts // world, world,
+              within.data_ptr(), counts.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    w_ref, c_ref, _ = local_route(idx, world, experts)
     assert torch.equal(within, w_ref) and torch.equal(counts, c_ref)
 
 
