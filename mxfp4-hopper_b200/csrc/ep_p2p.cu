@@ -95,122 +95,135 @@ __global__ void ep_barrier_kernel(const uint64_t* __restrict__ bases, mxb_ep_lay
   if (threadIdx.x < 32) barrier_warp(bases, L, epoch);
 }
 
-// Q-row of one 32-element block (fast path; literal fallback for Inf/NaN).
-__device__ __forceinline__ void p2p_quant_block(const uint32_t (&w)[16], uint32_t (&out)[4],
-                                                uint32_t& byte) {
+// Q-row of one 32-element block held by 4 consecutive lanes, 8 elements each
+// (fast path; literal fallback for Inf/NaN).  Returns this lane's 8 codes;
+// `byte` is the block's E8M0 scale (same in the 4 lanes).  The 4 lanes take
+// the same branch, so the shuffles name only their quad.
+__device__ __forceinline__ uint32_t p2p_quant_quad(const uint4 a, uint32_t& byte) {
+  const unsigned qmask = 0xFu << (threadIdx.x & 28);
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
   uint32_t m = 0;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) m = vmax_u16x2(m, w[i] & 0x7FFF7FFFu);
+  for (int i = 0; i < 4; ++i) m = vmax_u16x2(m, w[i] & 0x7FFF7FFFu);
+  m = vmax_u16x2(m, __shfl_xor_sync(qmask, m, 1));
+  m = vmax_u16x2(m, __shfl_xor_sync(qmask, m, 2));
   const uint32_t mb = max(m & 0xFFFFu, m >> 16);
   if (mb < 0x7F80u) {
     int k = (int)(mb >> 7) - 129 + ((mb & 0x7Fu) > 0x40u ? 1 : 0);
     k = k < -33 ? -33 : k;
     byte = (uint32_t)(k + 127);
     const float inv = __uint_as_float((uint32_t)(127 - k) << 23);
+    float v[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float v[8];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        v[2 * j] = bf16lo_to_f(w[4 * i + j]) * inv;
-        v[2 * j + 1] = bf16hi_to_f(w[4 * i + j]) * inv;
-      }
-      out[i] = cvt_e2m1x8(v);
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = bf16lo_to_f(w[j]) * inv;
+      v[2 * j + 1] = bf16hi_to_f(w[j]) * inv;
     }
-  } else {
-    float a = 1e-10f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-      a = fmaxf(a, fmaxf(fabsf(bf16lo_to_f(w[i])), fabsf(bf16hi_to_f(w[i]))));
-    const float y = exp2f(ceilf(log2f(fmaxf(a / 6.0f, 1e-10f))));
-    byte = ((uint32_t)(int)log2f(y) + 127u) & 0xFFu;
-    const float inv = 1.0f / y;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint32_t r = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint32_t wj = w[4 * i + j / 2];
-        float q = (j & 1) ? bf16hi_to_f(wj) : bf16lo_to_f(wj);
-        q = fminf(fmaxf(q * inv, -6.0f), 6.0f);
-        const uint32_t b = __float_as_uint(q);
-        const uint32_t sign = b >> 28 & 0x8u;
-        uint32_t ex = (b >> 23) & 0xFFu, man = b & 0x7FFFFFu;
-        if (ex < 127u) {
-          const uint32_t sh = 126u - ex;
-          man = sh >= 32u ? 0u : ((0x400000u | (man >> 1)) >> sh);
-        }
-        ex = (ex > 126u ? ex : 126u) - 126u;
-        const uint32_t m2 = man >> 21;
-        const uint32_t inc = (m2 & 1u) & (((man & 0x1FFFFFu) != 0u) | ((m2 >> 1) & 1u));
-        uint32_t c = (((ex << 2) | m2) + inc) >> 1;
-        c = c > 7u ? 7u : c;
-        r |= (sign | c) << (4 * j);
-      }
-      out[i] = r;
-    }
+    return cvt_e2m1x8(v);
   }
+  float am = 1e-10f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) am = fmaxf(am, fmaxf(fabsf(bf16lo_to_f(w[i])), fabsf(bf16hi_to_f(w[i]))));
+  am = fmaxf(am, __shfl_xor_sync(qmask, am, 1));
+  am = fmaxf(am, __shfl_xor_sync(qmask, am, 2));
+  const float y = exp2f(ceilf(log2f(fmaxf(am / 6.0f, 1e-10f))));
+  byte = ((uint32_t)(int)log2f(y) + 127u) & 0xFFu;
+  const float inv = 1.0f / y;
+  uint32_t r = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t wj = w[j / 2];
+    float q = (j & 1) ? bf16hi_to_f(wj) : bf16lo_to_f(wj);
+    q = fminf(fmaxf(q * inv, -6.0f), 6.0f);
+    const uint32_t b = __float_as_uint(q);
+    const uint32_t sign = b >> 28 & 0x8u;
+    uint32_t ex = (b >> 23) & 0xFFu, man = b & 0x7FFFFFu;
+    if (ex < 127u) {
+      const uint32_t sh = 126u - ex;
+      man = sh >= 32u ? 0u : ((0x400000u | (man >> 1)) >> sh);
+    }
+    ex = (ex > 126u ? ex : 126u) - 126u;
+    const uint32_t m2 = man >> 21;
+    const uint32_t inc = (m2 & 1u) & (((man & 0x1FFFFFu) != 0u) | ((m2 >> 1) & 1u));
+    uint32_t c = (((ex << 2) | m2) + inc) >> 1;
+    c = c > 7u ? 7u : c;
+    r |= (sign | c) << (4 * j);
+  }
+  return r;
 }
 
-// One CTA per token (grid-stride): quantize the row once, store its wire row
-// and routing metadata into every destination's receive buffer.
+constexpr int kP2PWarps = kP2PThreads / 32;
+constexpr int kDispatchBatch = 4;  // 256-element steps per batch: 4 loads in flight per lane
+
+// One warp per token (grid-stride): quantize the row once, store its wire row
+// and routing metadata into every destination's receive buffer.  A step of
+// 256 elements is 8 blocks, 4 lanes per block; a batch of 4 steps gives 512
+// bytes of codes, staged in shared memory so that every lane stores 16 bytes
+// per destination.
 __global__ void __launch_bounds__(kP2PThreads) ep_dispatch_p2p_kernel(
     const uint8_t* __restrict__ x, int64_t T, const int32_t* __restrict__ within,
     const int64_t* __restrict__ topk_idx, const float* __restrict__ topk_w,
     const uint64_t* __restrict__ bases, mxb_ep_layout L, int parity) {
-  __shared__ int64_t dst_row[64];
-  __shared__ __align__(16) uint8_t scale_bytes[kMaxScaleBytes];
-  const int G = L.world, H = L.hidden;
-  const int64_t nb = H / 32, rb = H / 2 + H / 32;
+  __shared__ __align__(16) uint8_t scale_bytes[kP2PWarps][kMaxScaleBytes];
+  __shared__ __align__(16) uint32_t stage[kP2PWarps][32 * kDispatchBatch];
+  __shared__ int64_t dst_row[kP2PWarps][32];
+  const int G = L.world, H = L.hidden, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t rb = H / 2 + H / 32;
+  const int steps = H / 256;  // H is a multiple of 512
   const int32_t* cnt = cnt_of(bases, L, parity);
-  int64_t off = 0;  // thread g < G: rows that lower ranks send to g come first
-  if (threadIdx.x < G)
-    for (int s = 0; s < L.rank; ++s) off += cnt[s * G + threadIdx.x];
-  const int64_t b0 = threadIdx.x;
-  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+  int64_t off = 0;  // lane g < G: rows that lower ranks send to g come first
+  if (lane < G)
+    for (int s = 0; s < L.rank; ++s) off += cnt[s * G + lane];
+  uint8_t* sb = scale_bytes[warp];
+  uint32_t* st = stage[warp];
+  int64_t* dr = dst_row[warp];
+  for (int64_t t = (int64_t)blockIdx.x * kP2PWarps + warp; t < T;
+       t += (int64_t)gridDim.x * kP2PWarps) {
     const uint8_t* xr = x + t * H * 2;
-    uint4 a[4];
-    if (b0 < nb) {  // the first block's loads go out before the barrier
+    if (lane < G) {
+      const int32_t wi = within[t * G + lane];
+      dr[lane] = wi < 0 ? -1 : off + wi;
+    }
+    __syncwarp();
+    for (int s0 = 0; s0 < steps; s0 += kDispatchBatch) {
+      uint4 a[kDispatchBatch];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = ld_stream_v4(xr + b0 * 64 + i * 16);
-    }
-    if (threadIdx.x < G) {
-      const int32_t wi = within[t * G + threadIdx.x];
-      dst_row[threadIdx.x] = wi < 0 ? -1 : off + wi;
-    }
-    __syncthreads();
-    for (int64_t b = b0; b < nb; b += kP2PThreads) {
-      if (b != b0) {
+      for (int u = 0; u < kDispatchBatch; ++u)
+        if (s0 + u < steps) a[u] = ld_stream_v4(xr + ((int64_t)(s0 + u) * 256 + lane * 8) * 2);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) a[i] = ld_stream_v4(xr + b * 64 + i * 16);
+      for (int u = 0; u < kDispatchBatch; ++u) {
+        if (s0 + u >= steps) continue;
+        uint32_t byte;
+        st[u * 32 + lane] = p2p_quant_quad(a[u], byte);
+        if ((lane & 3) == 0) sb[(s0 + u) * 8 + (lane >> 2)] = (uint8_t)byte;
       }
-      const uint32_t w[16] = {a[0].x, a[0].y, a[0].z, a[0].w, a[1].x, a[1].y, a[1].z, a[1].w,
-                              a[2].x, a[2].y, a[2].z, a[2].w, a[3].x, a[3].y, a[3].z, a[3].w};
-      uint32_t out[4], byte;
-      p2p_quant_block(w, out, byte);
-      scale_bytes[b] = (uint8_t)byte;
-      for (int g = 0; g < G; ++g) {
-        const int64_t r = dst_row[g];
-        if (r < 0) continue;
-        uint8_t* row = peer(bases, g) + L.wire_off + r * rb;
-        *reinterpret_cast<uint4*>(row + b * 16) = make_uint4(out[0], out[1], out[2], out[3]);
+      __syncwarp();
+      const int nbytes = min(kDispatchBatch, steps - s0) * 128;
+      if (lane * 16 < nbytes) {
+        const uint4 v = reinterpret_cast<const uint4*>(st)[lane];
+        for (int g = 0; g < G; ++g) {
+          const int64_t r = dr[g];
+          if (r < 0) continue;
+          uint8_t* row = peer(bases, g) + L.wire_off + r * rb;
+          *reinterpret_cast<uint4*>(row + (int64_t)s0 * 128 + lane * 16) = v;
+        }
       }
+      __syncwarp();
     }
-    __syncthreads();
-    // the row's scale bytes go out as 16-byte stores (H / 32 is a multiple of 16)
-    const int nv = (int)(nb / 16);
-    for (int i = threadIdx.x; i < G * nv; i += kP2PThreads) {
+    // the row's scale bytes as 16-byte stores (H / 32 is a multiple of 16)
+    const int nv = H / 512;
+    for (int i = lane; i < G * nv; i += 32) {
       const int g = i / nv, q = i - g * nv;
-      const int64_t r = dst_row[g];
+      const int64_t r = dr[g];
       if (r < 0) continue;
       uint8_t* row = peer(bases, g) + L.wire_off + r * rb;
       *reinterpret_cast<uint4*>(row + H / 2 + q * 16) =
-          *reinterpret_cast<const uint4*>(scale_bytes + q * 16);
+          *reinterpret_cast<const uint4*>(sb + q * 16);
     }
     // routing metadata: expert id local to the destination (or -1), weight (or 0)
-    for (int i = threadIdx.x; i < G * L.topk; i += kP2PThreads) {
+    for (int i = lane; i < G * L.topk; i += 32) {
       const int g = i / L.topk, j = i - g * L.topk;
-      const int64_t r = dst_row[g];
+      const int64_t r = dr[g];
       if (r < 0) continue;
       const int64_t e = topk_idx[t * L.topk + j];
       const bool here = e / L.experts_per_rank == g;
@@ -218,84 +231,83 @@ __global__ void __launch_bounds__(kP2PThreads) ep_dispatch_p2p_kernel(
       m[j] = here ? (int32_t)(e - (int64_t)g * L.experts_per_rank) : -1;
       m[L.topk + j] = __float_as_int(here ? topk_w[t * L.topk + j] : 0.0f);
     }
-    __syncthreads();
+    __syncwarp();
   }
   __threadfence_system();
 }
+
+constexpr int kReturnBatch = 4;  // chunks per lane with their loads issued together
 
 // Expert stage + return: for every received row r (source s, i-th row from s),
 // y = user row y_in[r] if given, else the routing-weighted identity expert
 // bf16(bf16(dequant(wire[r])) * sum_j weight[r][j]); the row is stored into
 // source s's `back` buffer at s's send slot sum_{g < rank} cnt[s][g] + i.
+// One warp per row; lane l handles the 8-element chunks l, l + 32, ...
+// Rows are visited source-minor (i -> j = i / G, s = i % G) so that at any
+// moment the warps write to every source, local HBM and NVLink together.
 __global__ void __launch_bounds__(kP2PThreads) ep_return_p2p_kernel(
     const uint8_t* __restrict__ y_in, const uint64_t* __restrict__ bases, mxb_ep_layout L,
     int parity) {
-  __shared__ int32_t col[64];     // cnt[s][rank]
+  __shared__ int32_t col[64];       // cnt[s][rank]
+  __shared__ int64_t start[64];     // sum_{q < s} cnt[q][rank]
   __shared__ int64_t back_off[64];  // sum_{g < rank} cnt[s][g]
-  const int G = L.world, H = L.hidden;
+  const int G = L.world, H = L.hidden, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t rb = H / 2 + H / 32;
   const int32_t* cnt = cnt_of(bases, L, parity);
   if (threadIdx.x < G) {
     const int s = threadIdx.x;
     col[s] = cnt[s * G + L.rank];
-    int64_t o = 0;
+    int64_t o = 0, st = 0;
     for (int g = 0; g < L.rank; ++g) o += cnt[s * G + g];
+    for (int q = 0; q < s; ++q) st += cnt[q * G + L.rank];
     back_off[s] = o;
+    start[s] = st;
   }
   __syncthreads();
-  // Rows are visited source-minor (i -> j = i / G, s = i % G) so that at any
-  // moment the CTAs write to every source, local HBM and NVLink together.
   int64_t cmax = 0;
   for (int s = 0; s < G; ++s) cmax = max(cmax, (int64_t)col[s]);
   const uint8_t* wire = peer(bases, L.rank) + L.wire_off;
   const int32_t* meta = reinterpret_cast<const int32_t*>(peer(bases, L.rank) + L.meta_off);
-  const int64_t chunks = H / 8;
-  for (int64_t i = blockIdx.x; i < cmax * G; i += gridDim.x) {
+  const int chunks = H / 8;  // a multiple of 64
+  for (int64_t i = (int64_t)blockIdx.x * kP2PWarps + warp; i < cmax * G;
+       i += (int64_t)gridDim.x * kP2PWarps) {
     const int s = (int)(i % G);
     const int64_t j = i / G;
     if (j >= col[s]) continue;
-    int64_t start = 0;
-    for (int q = 0; q < s; ++q) start += col[q];
-    const int64_t r = start + j;
-    const int64_t dst = back_off[s] + j;
-    uint8_t* out = peer(bases, s) + L.back_off + dst * H * 2;
-    float wsum = 0.0f;
-    if (!y_in) {  // lane j loads weight j; the sum keeps the order j = 0, 1, ...
-      const int32_t* m = meta + r * 2 * L.topk;
-      const int lane = threadIdx.x & 31;
-      const float wj = lane < L.topk ? __int_as_float(m[L.topk + lane]) : 0.0f;
-      wsum = __shfl_sync(0xffffffffu, wj, 0);
-      for (int j = 1; j < L.topk; ++j) wsum += __shfl_sync(0xffffffffu, wj, j);
-    }
-    const uint8_t* row = wire + r * rb;
-    constexpr int kU = 4;  // chunks per thread with their loads issued together
-    for (int64_t c0 = threadIdx.x; c0 < chunks; c0 += kP2PThreads * kU) {
-      if (y_in) {
-        uint4 v[kU];
+    const int64_t r = start[s] + j;
+    uint8_t* out = peer(bases, s) + L.back_off + (back_off[s] + j) * H * 2;
+    if (y_in) {
+      const uint8_t* yr = y_in + r * H * 2;
+      for (int c0 = lane; c0 < chunks; c0 += 32 * kReturnBatch) {
+        uint4 v[kReturnBatch];
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const int64_t c = c0 + u * kP2PThreads;
-          if (c < chunks) v[u] = *reinterpret_cast<const uint4*>(y_in + (r * H + c * 8) * 2);
-        }
+        for (int u = 0; u < kReturnBatch; ++u)
+          if (c0 + 32 * u < chunks) v[u] = *reinterpret_cast<const uint4*>(yr + (c0 + 32 * u) * 16);
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const int64_t c = c0 + u * kP2PThreads;
-          if (c < chunks) *reinterpret_cast<uint4*>(out + c * 16) = v[u];
-        }
-        continue;
+        for (int u = 0; u < kReturnBatch; ++u)
+          if (c0 + 32 * u < chunks) *reinterpret_cast<uint4*>(out + (c0 + 32 * u) * 16) = v[u];
       }
-      uint32_t wv[kU], ev[kU];
+      continue;
+    }
+    // lane j loads weight j; the sum keeps the order j = 0, 1, ...
+    const int32_t* m = meta + r * 2 * L.topk;
+    const float wj = lane < L.topk ? __int_as_float(m[L.topk + lane]) : 0.0f;
+    float wsum = __shfl_sync(0xffffffffu, wj, 0);
+    for (int q = 1; q < L.topk; ++q) wsum += __shfl_sync(0xffffffffu, wj, q);
+    const uint8_t* row = wire + r * rb;
+    for (int c0 = lane; c0 < chunks; c0 += 32 * kReturnBatch) {
+      uint32_t wv[kReturnBatch], ev[kReturnBatch];
 #pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int64_t c = c0 + u * kP2PThreads;
+      for (int u = 0; u < kReturnBatch; ++u) {
+        const int c = c0 + 32 * u;
         if (c < chunks) {
           wv[u] = *reinterpret_cast<const uint32_t*>(row + c * 4);
           ev[u] = row[H / 2 + (c >> 2)];
         }
       }
 #pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int64_t c = c0 + u * kP2PThreads;
+      for (int u = 0; u < kReturnBatch; ++u) {
+        const int c = c0 + 32 * u;
         if (c >= chunks) continue;
         const uint32_t w = wv[u], e = ev[u];
         uint32_t o[4];
@@ -304,16 +316,16 @@ __global__ void __launch_bounds__(kP2PThreads) ep_return_p2p_kernel(
         if (e - 2u <= 252u) {
           const uint32_t s2 = (e << 7) | (e << 23);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) o[i] = mul_bf16x2(o[i], s2);
+          for (int q = 0; q < 4; ++q) o[q] = mul_bf16x2(o[q], s2);
         } else {
           const float sc = e8m0_to_f(e);
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            o[i] = cvt_bf16x2(bf16lo_to_f(o[i]) * sc, bf16hi_to_f(o[i]) * sc);
+          for (int q = 0; q < 4; ++q)
+            o[q] = cvt_bf16x2(bf16lo_to_f(o[q]) * sc, bf16hi_to_f(o[q]) * sc);
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          o[i] = cvt_bf16x2(bf16lo_to_f(o[i]) * wsum, bf16hi_to_f(o[i]) * wsum);
+        for (int q = 0; q < 4; ++q)
+          o[q] = cvt_bf16x2(bf16lo_to_f(o[q]) * wsum, bf16hi_to_f(o[q]) * wsum);
         *reinterpret_cast<uint4*>(out + c * 16) = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
@@ -469,11 +481,14 @@ __global__ void __launch_bounds__(kRouteThreads) ep_route_serial_kernel(
 }
 
 // Local combine of the rows returned to this rank: out[t] = bf16(sum over g of
-// float(back[slot(t, g)])), slot(t, g) = sum_{g' < g} send_counts[g'] + within[t, g].
-// Work items are (token, 8-element chunk) pairs over a grid-stride loop with
-// no barrier inside; the slot offsets sit in shared memory and the loads of up
-// to 4 sources are issued before their sums.
-__global__ void __launch_bounds__(kP2PThreads) ep_p2p_combine_kernel(
+// float(back[slot(t, g)])), slot(t, g) = sum_{g' < g} send_counts[g'] + within[t, g],
+// the sum in the order g = 0, 1, ...  One warp per (token, segment of 128
+// 8-element chunks); lane l handles the chunks l, l + 32, l + 64, l + 96 of
+// the segment, with their 4 loads of a source issued together.  Sources that
+// sent the token nothing are skipped (a warp-uniform test).
+constexpr int kCombineBatch = 4;
+
+__global__ void __launch_bounds__(kP2PThreads, 4) ep_p2p_combine_kernel(
     const uint8_t* __restrict__ back, int64_t T, int64_t H, const int32_t* __restrict__ within,
     const int32_t* __restrict__ send_counts, int G, uint8_t* __restrict__ out) {
   __shared__ int64_t off[64];
@@ -485,39 +500,48 @@ __global__ void __launch_bounds__(kP2PThreads) ep_p2p_combine_kernel(
     }
   }
   __syncthreads();
-  const int64_t chunks = H / 8, n = T * chunks;
-  const bool small = n <= 0x7FFFFFFFLL;
-  for (int64_t i = (int64_t)blockIdx.x * kP2PThreads + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * kP2PThreads) {
-    const int64_t t = small ? (int64_t)((uint32_t)i / (uint32_t)chunks) : i / chunks;
-    const int64_t c = i - t * chunks;
-    const int32_t* wt = within + t * G;
-    // A source that sent nothing adds +0, which leaves the sum unchanged: it
-    // starts at +0 and so is never -0.
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int g0 = 0; g0 < G; g0 += 4) {
-      int32_t wi[4];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t chunks = H / 8, segs = (chunks + 32 * kCombineBatch - 1) / (32 * kCombineBatch);
+  for (int64_t i = (int64_t)blockIdx.x * kP2PWarps + warp; i < T * segs;
+       i += (int64_t)gridDim.x * kP2PWarps) {
+    const int64_t t = i / segs, c0 = (i - t * segs) * 32 * kCombineBatch + lane;
+    auto slot = [&](int g) -> int64_t {  // the row of source g, or -1
+      const int32_t wi = within[t * G + g];
+      return wi < 0 ? -1 : off[g] + wi;
+    };
+    const int64_t my_slot = lane < G ? slot(lane) : -1;
+    float acc[kCombineBatch][8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) wi[u] = g0 + u < G ? wt[g0 + u] : -1;
-      uint4 v[4];
+    for (int u = 0; u < kCombineBatch; ++u)
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        v[u] = wi[u] < 0 ? make_uint4(0, 0, 0, 0)
-                         : *reinterpret_cast<const uint4*>(
-                               back + ((off[g0 + u] + wi[u]) * H + c * 8) * 2);
+      for (int q = 0; q < 8; ++q) acc[u][q] = 0.0f;
+    for (int g = 0; g < G; ++g) {
+      const int64_t sl = g < 32 ? __shfl_sync(0xffffffffu, my_slot, g) : slot(g);
+      if (sl < 0) continue;
+      const uint8_t* src = back + sl * H * 2;
+      uint4 v[kCombineBatch];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kCombineBatch; ++u)
+        if (c0 + 32 * u < chunks) v[u] = *reinterpret_cast<const uint4*>(src + (c0 + 32 * u) * 16);
+#pragma unroll
+      for (int u = 0; u < kCombineBatch; ++u) {
+        if (c0 + 32 * u >= chunks) continue;
         const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          acc[2 * q] += bf16lo_to_f(w[q]);
-          acc[2 * q + 1] += bf16hi_to_f(w[q]);
+          acc[u][2 * q] += bf16lo_to_f(w[q]);
+          acc[u][2 * q + 1] += bf16hi_to_f(w[q]);
         }
       }
     }
-    *reinterpret_cast<uint4*>(out + (t * H + c * 8) * 2) =
-        make_uint4(cvt_bf16x2(acc[0], acc[1]), cvt_bf16x2(acc[2], acc[3]),
-                   cvt_bf16x2(acc[4], acc[5]), cvt_bf16x2(acc[6], acc[7]));
+    uint8_t* o = out + t * H * 2;
+#pragma unroll
+    for (int u = 0; u < kCombineBatch; ++u) {
+      if (c0 + 32 * u >= chunks) continue;
+      *reinterpret_cast<uint4*>(o + (c0 + 32 * u) * 16) =
+          make_uint4(cvt_bf16x2(acc[u][0], acc[u][1]), cvt_bf16x2(acc[u][2], acc[u][3]),
+                     cvt_bf16x2(acc[u][4], acc[u][5]), cvt_bf16x2(acc[u][6], acc[u][7]));
+    }
   }
 }
 
@@ -536,8 +560,10 @@ PFN_getAddressRange address_range_fn() {
   return fn;
 }
 
-int p2p_grid(int64_t rows) {
-  return (int)(rows < 148LL * 8 ? (rows > 0 ? rows : 1) : 148LL * 8);
+// CTAs for `items` warp-sized work items: one per item up to 8 CTAs per SM.
+int p2p_grid(int64_t items) {
+  const int64_t ctas = (items + kP2PWarps - 1) / kP2PWarps;
+  return (int)(ctas < 148LL * 8 ? (ctas > 0 ? ctas : 1) : 148LL * 8);
 }
 
 mxb_status check_layout(const mxb_ep_layout* L, const char* what) {
@@ -706,7 +732,8 @@ extern "C" mxb_status mxb_ep_p2p_combine(const void* back, int64_t T, int64_t H,
               "ep_p2p_combine: null pointer");
   MXB_REQUIRE(aligned(back, 16) && aligned(out, 16), MXB_ERR_MISALIGNED,
               "ep_p2p_combine: back and out must be 16-byte aligned");
-  ep_p2p_combine_kernel<<<p2p_grid(T), kP2PThreads, 0, to_cuda(stream)>>>(
+  const int64_t segs = (H / 8 + 127) / 128;
+  ep_p2p_combine_kernel<<<p2p_grid(T * segs), kP2PThreads, 0, to_cuda(stream)>>>(
       (const uint8_t*)back, T, H, within, send_counts, world, (uint8_t*)out);
   return launch_status("ep_p2p_combine");
 }
