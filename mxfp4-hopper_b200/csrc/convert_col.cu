@@ -702,16 +702,25 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
         qs = (amax > 1e-9f) ? (448.0f / amax) : 0.0f;
       } else {
         const float amax = mxv;  // initialised to 0 on the split path
-        float s;
+        // s = (float)(1 / (double)x) with x = 2^ceil(log2(amax / 448)) as the
+        // float with biased exponent ex (0 or Inf at the ends), and the stored
+        // scale 1 / s, which is x again; both from exponent bits, no division
+        float s, inv_s;
         if (amax <= eps) {
           s = 1.0f;
+          inv_s = 1.0f;
         } else {
           const uint32_t rbits = __float_as_uint(amax / 448.0f);
           uint32_t ex = (rbits >> 23) & 0xFFu;
           if (rbits & 0x7FFFFFu) ex += 1u;
-          s = (float)(1.0 / (double)__uint_as_float(ex << 23));
+          inv_s = __uint_as_float(ex << 23);  // x: 0 for ex = 0, Inf for ex = 255
+          const uint32_t sb = ex == 0u     ? 0x7F800000u             // 1 / 0
+                              : ex <= 253u ? (254u - ex) << 23       // 2^(127 - ex), normal
+                              : ex == 254u ? 0x00400000u             // 2^-127, subnormal
+                                           : 0u;                     // 1 / Inf
+          s = __uint_as_float(sb);
         }
-        if (t < g.cols) scales_out[g.scale_row * N + g.col0 + t] = 1.0f / s;
+        if (t < g.cols) scales_out[g.scale_row * N + g.col0 + t] = inv_s;
         qs = s;
       }
       col_qs[t] = qs;
@@ -788,10 +797,16 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
       }
     }
     if (!has_next) return;
-    // tile i+1's factors; that buffer was last read in tile i-1's step 1
-    if (t < 128) special_next = colT_factors(sc_next, gn, t, fac + ((i + 1) & 1) * 512);
+    // tile i+1 (on the split path rebuilt from its walk position, so that its
+    // descriptor is not kept live through the tile: 128 registers with no
+    // spills) and its factors; that buffer was last read in tile i-1's step 1
     w = wn;
-    g = gn;
+    if constexpr (kSplit) {
+      split_tile(w, N, sa, g);
+    } else {
+      g = gn;
+    }
+    if (t < 128) special_next = colT_factors(sc_next, g, t, fac + ((i + 1) & 1) * 512);
   }
   // Left early (tile `issued - 2` or `issued - 1` never arrived): do not exit
   // while a requested copy may still land in this CTA's memory.
