@@ -435,7 +435,8 @@ def time_other_ops(dev, stream, peak, only=None):
         res[name] = {"us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
 
     C3 = ("dequant_bf16_config3", "mxfp4_to_fp8_rows_config3", "mxfp4_to_fp8_col_config3",
-          "mxfp4_to_fp8_colT_config3", "mxfp4_to_fp8_colT_msplit8_config3")
+          "mxfp4_to_fp8_colT_config3", "mxfp4_to_fp8_colT_msplit8_config3",
+          "mxfp4_to_fp8_colT_msplit8x128_config3")
     # Q-row alone on config 2
     if want("quant_rows_config2", "quant_fused_fp8_config2", "swiglu_quant_config2"):
         _ops_config2(dev, sh, timeit, capi, syn)
@@ -503,26 +504,29 @@ def _ops_config3(dev, sh, timeit, capi, syn):
                           2 * Kb3, f8.data_ptr(), fcs.data_ptr(), 1e-10, sh),
         M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fcs.numel() * 4)
     # colT-split: config 3's rows as 8 ragged expert segments (seeded sizes, not
-    # multiples of 128, summing to M3), the grouped-GEMM wgrad operand
+    # multiples of 128, summing to M3), the grouped-GEMM wgrad operand; and the same
+    # shares rounded to multiples of 128 (every output row 16-byte aligned)
     gsz = torch.Generator().manual_seed(7)
     wts = torch.rand(8, generator=gsz) + 0.5
-    m_splits = (wts / wts.sum() * M3).floor().to(torch.int64).tolist()
-    m_splits[-1] += M3 - sum(m_splits)
-    so, sco, acc, accs = [], [], 0, 0
-    for m in m_splits:
-        so.append(acc)
-        sco.append(accs)
-        acc += m
-        accs += (m + 127) // 128
-    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
-    dm, dso, dsco = i32(m_splits), i32(so), i32(sco)
-    fss = torch.empty(accs, 2 * Kb3, dtype=torch.float32, device=dev)
-    timeit("mxfp4_to_fp8_colT_msplit8_config3",
-        lambda: capi.call("mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit", c.data_ptr(),
-                          sc.data_ptr(), M3, 2 * Kb3, f8.data_ptr(), fss.data_ptr(),
-                          dm.data_ptr(), dso.data_ptr(), dsco.data_ptr(), len(m_splits),
-                          max(m_splits), 1e-10, sh),
-        M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fss.numel() * 4)
+    for name, q in (("mxfp4_to_fp8_colT_msplit8_config3", 1),
+                    ("mxfp4_to_fp8_colT_msplit8x128_config3", 128)):
+        m_splits = ((wts / wts.sum() * M3 / q).floor() * q).to(torch.int64).tolist()
+        m_splits[-1] += M3 - sum(m_splits)
+        so, sco, acc, accs = [], [], 0, 0
+        for m in m_splits:
+            so.append(acc)
+            sco.append(accs)
+            acc += m
+            accs += (m + 127) // 128
+        i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
+        dm, dso, dsco = i32(m_splits), i32(so), i32(sco)
+        fss = torch.empty(accs, 2 * Kb3, dtype=torch.float32, device=dev)
+        timeit(name,
+            lambda: capi.call("mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit", c.data_ptr(),
+                              sc.data_ptr(), M3, 2 * Kb3, f8.data_ptr(), fss.data_ptr(),
+                              dm.data_ptr(), dso.data_ptr(), dsco.data_ptr(), len(m_splits),
+                              max(m_splits), 1e-10, sh),
+            M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fss.numel() * 4)
 
 
 def _ops_permute(dev, sh, timeit, capi, syn):
