@@ -527,6 +527,13 @@ bool fast_params(float eps, float fp4_min, float fp4_max) {
   return fp4_max == 6.0f && fp4_min == -6.0f && eps >= 0.0f && eps <= 6e-10f;
 }
 
+// Hardware approximate reciprocal (about 1 ulp), subnormal results kept.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // ------------------------------------------------- SwiGLU fused with Q-row
 // Megatron's SwiGLU with fp4_input_store (megatron-0.15.0rc7.diff:164-193)
 // returns swiglu(x) = silu(x1) * x2 (x1, x2 the two halves of the last
@@ -548,22 +555,34 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const __nv_bfloat16* 
   const unsigned pair_mask = 3u << (lane & ~1);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t K = 2 * H;         // row length of x
-  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < halves;
-       base += stride) {
+  // the 2 x 32 input bytes of work item h (gate and up half-blocks), loaded one
+  // item ahead so that the loads overlap the previous item's arithmetic
+  auto load_item = [&](int64_t h, uint32_t (&w)[2][8]) {
+    const int64_t pr = h >> 1, r = pr / J, j = pr - r * J;
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const uint8_t* src =
+          reinterpret_cast<const uint8_t*>(x + r * K + s * H + j * 32 + (h & 1) * 16);
+      const uint4 a = ld_stream_v4(src), b = ld_stream_v4(src + 16);
+      w[s][0] = a.x; w[s][1] = a.y; w[s][2] = a.z; w[s][3] = a.w;
+      w[s][4] = b.x; w[s][5] = b.y; w[s][6] = b.z; w[s][7] = b.w;
+    }
+  };
+  int64_t base = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31);
+  uint32_t nxt[2][8];
+  if (base + lane < halves) load_item(base + lane, nxt);
+  for (; base < halves; base += stride) {
     const int64_t h = base + lane;
+    uint32_t wv[2][8];  // [gate, up][16 elements as BF16 pairs]
+#pragma unroll
+    for (int s = 0; s < 2; ++s)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wv[s][i] = nxt[s][i];
+    if (base + stride + lane < halves) load_item(base + stride + lane, nxt);
     if (h >= halves) continue;  // pairs are both in or both out (halves is even)
     const int64_t pr = h >> 1;
     const int half = (int)(h & 1);
     const int64_t r = pr / J, j = pr - r * J;
-    uint32_t wv[2][8];  // [gate, up][16 elements as BF16 pairs]
-#pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      const uint8_t* src =
-          reinterpret_cast<const uint8_t*>(x + r * K + s * H + j * 32 + half * 16);
-      const uint4 a = ld_stream_v4(src), b = ld_stream_v4(src + 16);
-      wv[s][0] = a.x; wv[s][1] = a.y; wv[s][2] = a.z; wv[s][3] = a.w;
-      wv[s][4] = b.x; wv[s][5] = b.y; wv[s][6] = b.z; wv[s][7] = b.w;
-    }
     // ---- MXFP4 of both blocks (bit-exact Q-row)
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
@@ -600,10 +619,11 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const __nv_bfloat16* 
       for (int e = 0; e < 2; ++e) {
         const float g = e ? bf16hi_to_f(wv[0][i]) : bf16lo_to_f(wv[0][i]);
         const float u = e ? bf16hi_to_f(wv[1][i]) : bf16lo_to_f(wv[1][i]);
-        // g * u * (1 / (1 + e^-g)): the hardware exponential and a correctly
-        // rounded reciprocal keep the relative error near 1e-6, far inside one
-        // BF16 ulp; e^-g = Inf gives (g * u) * +0, keeping the sign of zero
-        v[e] = (g * u) * __frcp_rn(1.0f + __expf(-g));
+        // g * u * (1 / (1 + e^-g)): the hardware exponential and reciprocal
+        // (rcp.approx.f32, subnormal results kept) keep the relative error
+        // near 1e-6, far inside one BF16 ulp; e^-g = Inf gives (g * u) * +0,
+        // keeping the sign of zero
+        v[e] = (g * u) * rcp_approx(1.0f + __expf(-g));
       }
       o[i] = cvt_bf16x2(v[0], v[1]);
     }
