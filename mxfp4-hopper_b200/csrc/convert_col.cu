@@ -66,7 +66,13 @@ __device__ __forceinline__ bool load_code_tile(uint8_t* tile, uint64_t* bar, con
 // neighbouring lanes transpose their 4x4 byte blocks with two shuffles so each
 // lane stores four rows of one element as one word of the transposed tile,
 // which leaves as 128-byte runs of output rows.
-constexpr int kColPitch = 160;                 // bytes per element row of the transposed tile
+// The transposed tile has 128-byte element rows whose 16-byte chunks are
+// XOR-swizzled by (element & 3) << 1: the four lanes that write four element
+// rows of the same 4-byte column, and the two half-warps, land in eight
+// different chunks (no bank conflicts), and the 8 lanes that read one element
+// row read a permutation of its chunks.  50 KB of shared memory per CTA: four
+// CTAs per SM.
+constexpr int kColPitch = 128;                 // bytes per element row of the transposed tile
 constexpr uint32_t kColCodeBytes = 128 * 128;  // 16 KiB
 constexpr size_t kColSmem = 1024 + kColCodeBytes + 256 * kColPitch + 4 * 8 + 16;
 
@@ -116,8 +122,10 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
   // lane-dependent byte selectors of the two transpose rounds
   const uint32_t sel1 = (lane & 2) ? 0x3276u : 0x5410u;
   const uint32_t sel2 = (lane & 1) ? 0x3715u : 0x6240u;
-  // this lane stores element (4k + (lane & 3)) for rows (lane & ~3) .. +3
-  uint8_t* trl = tr + (lane & 3) * kColPitch + rb * 32 + (lane & ~3);
+  // this lane stores element (4k + (lane & 3)) for rows (lane & ~3) .. +3: byte
+  // column rb * 32 + (lane & ~3), chunk rb * 2 + lane / 16 swizzled by (lane & 3) << 1
+  uint8_t* trl = tr + (lane & 3) * kColPitch +
+                 ((((rb * 2 + (lane >> 4)) ^ ((lane & 3) << 1))) << 4) + ((lane >> 2) & 3) * 4;
 
 #pragma unroll
   for (int cc = 0; cc < 4; ++cc) {
@@ -150,7 +158,7 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
   for (int k = 0; k < 8; ++k) {
     const int i = k * kThreads + t;
     const int n = i >> 3, part = i & 7;
-    const uint4 o = *reinterpret_cast<const uint4*>(&tr[n * kColPitch + part * 16]);
+    const uint4 o = *reinterpret_cast<const uint4*>(&tr[n * kColPitch + ((part ^ ((n & 3) << 1)) << 4)]);
     st_stream_v4(ob + n * M + part * 16, o);
   }
 }
