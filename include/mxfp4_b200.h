@@ -46,9 +46,14 @@ const char* mxb_last_error(void);
 /* Library version string. */
 const char* mxb_version(void);
 /* Number of bounded pipeline waits that gave up on the current device since
- * the library was loaded (0 in correct operation; a non-zero value means a
- * kernel abandoned its work and its outputs are invalid).  Synchronises. */
+ * the library was loaded (or last reset), summed over every kernel of the
+ * library that waits on an mbarrier: the quantizers, the column / split FP8
+ * converters and the GEMM (0 in correct operation; a non-zero value means a
+ * kernel abandoned its work and its outputs are invalid).  Synchronises.
+ * 0xFFFFFFFF if the counters cannot be read. */
 unsigned int mxb_wait_timeouts(void);
+/* Returns mxb_wait_timeouts() and zeroes the counters on the current device. */
+unsigned int mxb_reset_wait_timeouts(void);
 
 /* ------------------------------------------------------------ quantize */
 
@@ -330,7 +335,16 @@ mxb_status mxb_ep_route(const int64_t* topk_idx, int64_t T, int32_t topk, int32_
 mxb_status mxb_ep_p2p_combine(const void* back, int64_t T, int64_t H, const int32_t* within,
                               const int32_t* send_counts, int32_t world, void* out,
                               mxb_stream_t stream);
+/* Cross-GPU waits (barriers, count exchange) that gave up on the current
+ * device since load or the last reset; a non-zero value means the step's
+ * outputs are invalid and a peer is late or gone.  Synchronises. */
 unsigned int mxb_ep_wait_timeouts(void);
+/* Returns mxb_ep_wait_timeouts() and zeroes the counter on the current device. */
+unsigned int mxb_ep_reset_wait_timeouts(void);
+/* Polls (each ~64 ns of sleep plus one system-scope load) a cross-GPU wait
+ * makes on the current device before it gives up; 0 restores the default
+ * 2^22 (~0.3 s).  Synchronous; set it between steps, not while a step runs. */
+mxb_status mxb_ep_set_wait_polls(uint32_t polls);
 
 #ifdef __cplusplus
 }

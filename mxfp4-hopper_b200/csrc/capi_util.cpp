@@ -5,6 +5,7 @@
 
 #include <mutex>
 #include <unordered_map>
+#include <vector>
 
 namespace mxb {
 
@@ -15,6 +16,32 @@ void set_error(const char* fmt, ...) {
   va_start(ap, fmt);
   vsnprintf(g_err, sizeof(g_err), fmt, ap);
   va_end(ap);
+}
+
+static std::mutex& reader_mu() {
+  static std::mutex m;
+  return m;
+}
+static std::vector<unsigned int (*)(bool)>& readers() {
+  static std::vector<unsigned int (*)(bool)> v;
+  return v;
+}
+
+bool register_wait_timeout_reader(unsigned int (*reader)(bool reset)) {
+  std::lock_guard<std::mutex> lk(reader_mu());
+  readers().push_back(reader);
+  return true;
+}
+
+unsigned int sum_wait_timeouts(bool reset) {
+  std::lock_guard<std::mutex> lk(reader_mu());
+  unsigned long long total = 0;
+  for (auto r : readers()) {
+    const unsigned int v = r(reset);
+    if (v == 0xFFFFFFFFu) return v;
+    total += v;
+  }
+  return total >= 0xFFFFFFFFull ? 0xFFFFFFFEu : (unsigned int)total;
 }
 
 int persistent_ctas(const void* kernel, int threads, size_t smem) {

@@ -39,6 +39,13 @@ bool make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType 
                         uint32_t box_rows,
                         CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
 
+// Registry of per-translation-unit wait-timeout counters (see tma.cuh).
+// Returns true so that it can initialise a namespace-scope constant.
+bool register_wait_timeout_reader(unsigned int (*reader)(bool reset));
+// Sum of every registered counter on the current device; with `reset` the
+// counters are zeroed after reading.  0xFFFFFFFF if a read failed.
+unsigned int sum_wait_timeouts(bool reset);
+
 // Number of resident CTAs worth launching for a grid-stride kernel.
 int persistent_ctas(const void* kernel, int threads, size_t smem);
 

@@ -957,22 +957,41 @@ extern "C" mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col(const void* input, co
   return launch_status("mxfp4_to_fp8_colT");
 }
 
-extern "C" mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit(
-    const void* input, const void* input_s, int64_t total_M, int64_t N, void* output_q,
-    void* output_s, const int32_t* m_splits, const int32_t* split_offsets,
-    const int32_t* scale_offsets, int64_t num_splits, int64_t max_split_len, float eps,
-    mxb_stream_t stream) {
+// Argument checks shared by both split entry points, so that the no-alloc
+// variant rejects a bad call before it touches its shared scratch.  Sets
+// *empty when there is nothing to convert (then MXB_OK and no launch).
+static mxb_status colT_msplit_check(const void* input, const void* input_s, int64_t total_M,
+                                    int64_t N, const void* output_q, const void* output_s,
+                                    const int32_t* m_splits, int64_t num_splits,
+                                    int64_t max_split_len, bool* empty) {
+  *empty = false;
   MXB_REQUIRE(total_M >= 0 && N >= 0 && N % 32 == 0 && num_splits >= 0 && max_split_len >= 0,
               MXB_ERR_INVALID_ARGUMENT, "mxfp4_to_fp8_colT_msplit: need N %% 32 == 0, got %lld",
               (long long)N);
   MXB_REQUIRE(num_splits <= 65535 && cdiv(max_split_len, 128) <= 65535, MXB_ERR_INVALID_ARGUMENT,
               "mxfp4_to_fp8_colT_msplit: too many splits or rows per split");
-  if (total_M == 0 || N == 0 || num_splits == 0 || max_split_len == 0) return MXB_OK;
-  MXB_REQUIRE(input && input_s && output_q && output_s && m_splits && split_offsets &&
-                  scale_offsets,
-              MXB_ERR_INVALID_ARGUMENT, "mxfp4_to_fp8_colT_msplit: null pointer");
+  if (total_M == 0 || N == 0 || num_splits == 0 || max_split_len == 0) {
+    *empty = true;
+    return MXB_OK;
+  }
+  MXB_REQUIRE(input && input_s && output_q && output_s && m_splits, MXB_ERR_INVALID_ARGUMENT,
+              "mxfp4_to_fp8_colT_msplit: null pointer");
   MXB_REQUIRE(aligned(input, 16), MXB_ERR_MISALIGNED,
               "mxfp4_to_fp8_colT_msplit: input not 16-byte aligned");
+  return MXB_OK;
+}
+
+extern "C" mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit(
+    const void* input, const void* input_s, int64_t total_M, int64_t N, void* output_q,
+    void* output_s, const int32_t* m_splits, const int32_t* split_offsets,
+    const int32_t* scale_offsets, int64_t num_splits, int64_t max_split_len, float eps,
+    mxb_stream_t stream) {
+  bool empty = false;
+  const mxb_status chk = colT_msplit_check(input, input_s, total_M, N, output_q, output_s, m_splits,
+                                           num_splits, max_split_len, &empty);
+  if (chk != MXB_OK || empty) return chk;
+  MXB_REQUIRE(split_offsets && scale_offsets, MXB_ERR_INVALID_ARGUMENT,
+              "mxfp4_to_fp8_colT_msplit: null pointer");
   MXB_REQUIRE(colT_attr(), MXB_ERR_CUDA, "mxfp4_to_fp8_colT_msplit: cannot reserve shared memory");
   CUtensorMap tmap;
   if (!make_tensor_map_2d(&tmap, input, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, total_M, N / 2, N / 2,
@@ -1016,8 +1035,10 @@ extern "C" mxb_status mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit_noalloc(
               (long long)num_splits, kMaxSeg);
   MXB_REQUIRE(total_M >= 0 && total_M <= INT32_MAX && max_split_len >= 0, MXB_ERR_INVALID_ARGUMENT,
               "mxfp4_to_fp8_colT_msplit_noalloc: need 0 <= total_M <= 2^31-1 and max_split_len >= 0");
-  if (total_M == 0 || N == 0 || num_splits == 0 || max_split_len == 0) return MXB_OK;
-  MXB_REQUIRE(m_splits, MXB_ERR_INVALID_ARGUMENT, "mxfp4_to_fp8_colT_msplit_noalloc: null m_splits");
+  bool empty = false;
+  const mxb_status chk = colT_msplit_check(input, input_s, total_M, N, output_q, output_s, m_splits,
+                                           num_splits, max_split_len, &empty);
+  if (chk != MXB_OK || empty) return chk;
   int32_t* scratch = msplit_scratch();
   MXB_REQUIRE(scratch, MXB_ERR_CUDA,
               "mxfp4_to_fp8_colT_msplit_noalloc: cannot look up the static scratch (%s)",

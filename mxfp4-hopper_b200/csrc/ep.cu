@@ -19,69 +19,18 @@
 
 #include "capi_util.h"
 #include "common.cuh"
+#include "qrow.cuh"
 
 namespace mxb {
 namespace {
 
 constexpr int kEpThreads = 256;
 
-// Q-row of one 32-element block held as 16 BF16 pairs (fast path: fp4_max = 6,
-// eps <= 6e-10), same arithmetic as the quantize kernels.
+// Q-row of one 32-element block held as 16 BF16 pairs (fp4_max = 6,
+// eps <= 6e-10): the quantizers' own block routine (qrow.cuh).
 __device__ __forceinline__ void ep_quant_block(const uint32_t (&w)[16], uint32_t (&out)[4],
                                                uint32_t& byte, float eps) {
-  uint32_t m = 0;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) m = vmax_u16x2(m, w[i] & 0x7FFF7FFFu);
-  const uint32_t mb = max(m & 0xFFFFu, m >> 16);
-  if (mb < 0x7F80u) {
-    int k = (int)(mb >> 7) - 129 + ((mb & 0x7Fu) > 0x40u ? 1 : 0);
-    k = k < -33 ? -33 : k;
-    byte = (uint32_t)(k + 127);
-    const float inv = __uint_as_float((uint32_t)(127 - k) << 23);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float v[8];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        v[2 * j] = bf16lo_to_f(w[4 * i + j]) * inv;
-        v[2 * j + 1] = bf16hi_to_f(w[4 * i + j]) * inv;
-      }
-      out[i] = cvt_e2m1x8(v);
-    }
-  } else {
-    // Inf / NaN in the block: the reference formula literally
-    float a = eps;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) a = fmaxf(a, fmaxf(fabsf(bf16lo_to_f(w[i])), fabsf(bf16hi_to_f(w[i]))));
-    float y = exp2f(ceilf(log2f(fmaxf(a / 6.0f, 1e-10f))));
-    byte = ((uint32_t)(int)log2f(y) + 127u) & 0xFFu;
-    const float inv = 1.0f / y;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint32_t r = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint32_t wj = w[4 * i + j / 2];
-        float q = (j & 1) ? bf16hi_to_f(wj) : bf16lo_to_f(wj);
-        q = fminf(fmaxf(q * inv, -6.0f), 6.0f);
-        // E2M1 RNE with the sign kept, the reference's integer rounding
-        const uint32_t b = __float_as_uint(q);
-        const uint32_t sign = b >> 28 & 0x8u;
-        uint32_t ex = (b >> 23) & 0xFFu, man = b & 0x7FFFFFu;
-        if (ex < 127u) {
-          const uint32_t sh = 126u - ex;
-          man = sh >= 32u ? 0u : ((0x400000u | (man >> 1)) >> sh);
-        }
-        ex = (ex > 126u ? ex : 126u) - 126u;
-        const uint32_t m2 = man >> 21;
-        const uint32_t inc = (m2 & 1u) & (((man & 0x1FFFFFu) != 0u) | ((m2 >> 1) & 1u));
-        uint32_t c = (((ex << 2) | m2) + inc) >> 1;
-        c = c > 7u ? 7u : c;
-        r |= (sign | c) << (4 * j);
-      }
-      out[i] = r;
-    }
-  }
+  quant_block32<true>(w, QuantParams{eps, -6.0f, 6.0f}, out, byte);
 }
 
 __global__ void __launch_bounds__(kEpThreads) ep_pack_kernel(const uint8_t* __restrict__ x,

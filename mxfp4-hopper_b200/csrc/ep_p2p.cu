@@ -26,12 +26,15 @@
 
 #include "capi_util.h"
 #include "common.cuh"
+#include "qrow.cuh"
 
 namespace mxb {
 namespace {
 
 static __device__ unsigned int g_ep_timeouts;
-constexpr uint32_t kPeerSpins = 1u << 22;  // polls of ~64 ns sleep each
+constexpr uint32_t kPeerSpins = 1u << 22;  // default polls of ~64 ns sleep each
+// Polls a cross-GPU wait makes before it gives up (mxb_ep_set_wait_polls).
+static __device__ uint32_t g_ep_wait_polls = kPeerSpins;
 constexpr int kP2PThreads = 256;
 constexpr int kMaxScaleBytes = 2048;  // H / 32 for H <= 65536
 
@@ -64,9 +67,10 @@ __device__ void barrier_warp(const uint64_t* bases, const mxb_ep_layout& L, uint
     st_release_sys(reinterpret_cast<uint32_t*>(peer(bases, q) + L.sig_off) + L.rank, epoch);
   for (int q = p; q < L.world; q += 32) {
     const uint32_t* mine = reinterpret_cast<const uint32_t*>(peer(bases, L.rank) + L.sig_off) + q;
+    const uint32_t limit = g_ep_wait_polls;
     uint32_t i = 0;
     while (ld_acquire_sys(mine) < epoch) {
-      if (++i == kPeerSpins) {
+      if (++i >= limit) {
         atomicAdd(&g_ep_timeouts, 1u);
         break;
       }
@@ -95,10 +99,11 @@ __global__ void ep_barrier_kernel(const uint64_t* __restrict__ bases, mxb_ep_lay
   if (threadIdx.x < 32) barrier_warp(bases, L, epoch);
 }
 
-// Q-row of one 32-element block held by 4 consecutive lanes, 8 elements each
-// (fast path; literal fallback for Inf/NaN).  Returns this lane's 8 codes;
-// `byte` is the block's E8M0 scale (same in the 4 lanes).  The 4 lanes take
-// the same branch, so the shuffles name only their quad.
+// Q-row of one 32-element block held by 4 consecutive lanes, 8 elements each,
+// with the quantizers' scale rule and rounding (qrow.cuh): fast path, or the
+// literal reference formula for blocks with Inf/NaN.  Returns this lane's 8
+// codes; `byte` is the block's E8M0 scale (same in the 4 lanes).  The 4 lanes
+// take the same branch, so the shuffles name only their quad.
 __device__ __forceinline__ uint32_t p2p_quant_quad(const uint4 a, uint32_t& byte) {
   const unsigned qmask = 0xFu << (threadIdx.x & 28);
   const uint32_t w[4] = {a.x, a.y, a.z, a.w};
@@ -109,47 +114,19 @@ __device__ __forceinline__ uint32_t p2p_quant_quad(const uint4 a, uint32_t& byte
   m = vmax_u16x2(m, __shfl_xor_sync(qmask, m, 2));
   const uint32_t mb = max(m & 0xFFFFu, m >> 16);
   if (mb < 0x7F80u) {
-    int k = (int)(mb >> 7) - 129 + ((mb & 0x7Fu) > 0x40u ? 1 : 0);
-    k = k < -33 ? -33 : k;
-    byte = (uint32_t)(k + 127);
-    const float inv = __uint_as_float((uint32_t)(127 - k) << 23);
-    float v[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      v[2 * j] = bf16lo_to_f(w[j]) * inv;
-      v[2 * j + 1] = bf16hi_to_f(w[j]) * inv;
-    }
-    return cvt_e2m1x8(v);
+    uint32_t inv;
+    scale_fast(mb, byte, inv);
+    return encode8_pairs(w, inv);
   }
-  float am = 1e-10f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) am = fmaxf(am, fmaxf(fabsf(bf16lo_to_f(w[i])), fabsf(bf16hi_to_f(w[i]))));
+  const QuantParams p{1e-10f, -6.0f, 6.0f};
+  uint32_t f[8];
+  unpack8(w, f);
+  float am = amax_generic(f, p.eps);
   am = fmaxf(am, __shfl_xor_sync(qmask, am, 1));
   am = fmaxf(am, __shfl_xor_sync(qmask, am, 2));
-  const float y = exp2f(ceilf(log2f(fmaxf(am / 6.0f, 1e-10f))));
-  byte = ((uint32_t)(int)log2f(y) + 127u) & 0xFFu;
-  const float inv = 1.0f / y;
-  uint32_t r = 0;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint32_t wj = w[j / 2];
-    float q = (j & 1) ? bf16hi_to_f(wj) : bf16lo_to_f(wj);
-    q = fminf(fmaxf(q * inv, -6.0f), 6.0f);
-    const uint32_t b = __float_as_uint(q);
-    const uint32_t sign = b >> 28 & 0x8u;
-    uint32_t ex = (b >> 23) & 0xFFu, man = b & 0x7FFFFFu;
-    if (ex < 127u) {
-      const uint32_t sh = 126u - ex;
-      man = sh >= 32u ? 0u : ((0x400000u | (man >> 1)) >> sh);
-    }
-    ex = (ex > 126u ? ex : 126u) - 126u;
-    const uint32_t m2 = man >> 21;
-    const uint32_t inc = (m2 & 1u) & (((man & 0x1FFFFFu) != 0u) | ((m2 >> 1) & 1u));
-    uint32_t c = (((ex << 2) | m2) + inc) >> 1;
-    c = c > 7u ? 7u : c;
-    r |= (sign | c) << (4 * j);
-  }
-  return r;
+  float inv;
+  scale_generic(am, p, inv, byte);
+  return encode8_generic(f, inv, p);
 }
 
 constexpr int kP2PWarps = kP2PThreads / 32;
@@ -742,4 +719,18 @@ extern "C" unsigned int mxb_ep_wait_timeouts(void) {
   unsigned int v = 0;
   if (cudaMemcpyFromSymbol(&v, g_ep_timeouts, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
   return v;
+}
+
+extern "C" unsigned int mxb_ep_reset_wait_timeouts(void) {
+  const unsigned int v = mxb_ep_wait_timeouts();
+  const unsigned int z = 0;
+  if (cudaMemcpyToSymbol(g_ep_timeouts, &z, sizeof(z)) != cudaSuccess) return 0xFFFFFFFFu;
+  return v;
+}
+
+extern "C" mxb_status mxb_ep_set_wait_polls(uint32_t polls) {
+  const uint32_t v = polls ? polls : kPeerSpins;
+  const cudaError_t e = cudaMemcpyToSymbol(g_ep_wait_polls, &v, sizeof(v));
+  MXB_REQUIRE(e == cudaSuccess, MXB_ERR_CUDA, "ep_set_wait_polls: %s", cudaGetErrorString(e));
+  return MXB_OK;
 }

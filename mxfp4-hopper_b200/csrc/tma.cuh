@@ -3,9 +3,11 @@
 // tile always comes from this GPU's own memory into this CTA's shared memory.
 //
 // Every wait is bounded.  A wait that runs out increments the including
-// file's g_mxb_wait_timeouts counter (reported by mxb_wait_timeouts()) and the
-// kernel abandons its remaining work after a second bounded wait for its own
-// copies in flight.
+// file's g_mxb_wait_timeouts counter and the kernel abandons its remaining
+// work after a second bounded wait for its own copies in flight.  Each
+// translation unit that includes this header has its own counter (device code
+// is not relocatable); a static registrar below adds a reader for it to the
+// library-wide list that mxb_wait_timeouts() sums.
 #pragma once
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -19,6 +21,21 @@ namespace mxb {
 
 // One counter per translation unit that uses these helpers.
 static __device__ unsigned int g_mxb_wait_timeouts;
+
+// Host: reads (and with `reset`, zeroes) this translation unit's counter on
+// the current device; 0xFFFFFFFF if the read fails.
+static unsigned int read_tu_wait_timeouts(bool reset) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_mxb_wait_timeouts, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  if (reset) {
+    const unsigned int z = 0;
+    if (cudaMemcpyToSymbol(g_mxb_wait_timeouts, &z, sizeof(z)) != cudaSuccess) return 0xFFFFFFFFu;
+  }
+  return v;
+}
+namespace {
+const bool g_tu_wait_reader_registered = register_wait_timeout_reader(&read_tu_wait_timeouts);
+}  // namespace
 
 constexpr uint32_t kWaitSpins = 1u << 24;  // try_wait rounds before giving up
 

@@ -70,6 +70,7 @@ SIGNATURES.update({
     "mxb_ep_p2p_return": [_P, _P, _LP, _I, _P],
     "mxb_ep_route": [_P, _I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, _P, _P],
     "mxb_ep_p2p_combine": [_P, _I64, _I64, _P, _P, ctypes.c_int32, _P, _P],
+    "mxb_ep_set_wait_polls": [_U32],
 })
 
 STATUS = {0: "MXB_OK", 1: "MXB_ERR_INVALID_ARGUMENT", 2: "MXB_ERR_MISALIGNED", 3: "MXB_ERR_CUDA",
@@ -100,7 +101,9 @@ def load() -> ctypes.CDLL:
         L.mxb_last_error.restype = ctypes.c_char_p
         L.mxb_version.restype = ctypes.c_char_p
         L.mxb_wait_timeouts.restype = ctypes.c_uint
+        L.mxb_reset_wait_timeouts.restype = ctypes.c_uint
         L.mxb_ep_wait_timeouts.restype = ctypes.c_uint
+        L.mxb_ep_reset_wait_timeouts.restype = ctypes.c_uint
         L.mxb_gemm_wait_timeouts.restype = ctypes.c_uint
         L.mxb_quant_mxfp4_rowcol_host_workspace.argtypes = [_I64, _I64, _I64]
         L.mxb_quant_mxfp4_rowcol_host_workspace.restype = ctypes.c_int64
@@ -126,7 +129,13 @@ def last_error() -> str:
 
 
 def wait_timeouts() -> int:
+    """Bounded waits that gave up on the current device, over every kernel
+    that waits on an mbarrier (quantizers, column converters, GEMM)."""
     return int(load().mxb_wait_timeouts())
+
+
+def reset_wait_timeouts() -> int:
+    return int(load().mxb_reset_wait_timeouts())
 
 
 def version() -> str:

@@ -27,6 +27,13 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
+
+
+def reference_root() -> Path:
+    """Where the reference checkout is: $MXFP4_REFERENCE_ROOT, else a directory
+    named `reference` next to this repository's own directory."""
+    env = os.environ.get("MXFP4_REFERENCE_ROOT")
+    return Path(env) if env else HERE.parent.parent / "reference"
 KERNELS = [
     "per_token_quant_mxfp4.cu",
     "per_token_Mxfp4ToBf16_dequant.cu",
@@ -102,7 +109,7 @@ def build(ref_root: Path, jobs: int = 6, verbose: bool = True) -> Path:
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("MXFP4_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--ref", default=str(reference_root()))
     ap.add_argument("-j", type=int, default=6)
     a = ap.parse_args()
     build(Path(a.ref), jobs=a.j)

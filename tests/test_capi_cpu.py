@@ -56,3 +56,23 @@ def test_empty_inputs_are_a_no_op():
     assert capi.status_of("mxb_per_token_group_quant_fp4", None, 0, 64, 64, None, None, 32, 1e-10,
                           -6.0, 6.0, 0, None) == 0
     assert capi.status_of("mxb_per_token_Mxfp4ToBf16_dequant", None, None, 0, 16, None, None) == 0
+
+
+@pytest.mark.parametrize("args", [
+    # N not a multiple of 32
+    (1, 1, 256, 40, 1, 1, 1, 2, 256, 1e-10, None),
+    # null input
+    (None, 1, 256, 64, 1, 1, 1, 2, 256, 1e-10, None),
+    # misaligned input
+    (17, 1, 256, 64, 1, 1, 1, 2, 256, 1e-10, None),
+    # too many rows per split for the grid
+    (1, 1, 256, 64, 1, 1, 1, 2, 128 * 65536, 1e-10, None),
+])
+def test_noalloc_split_rejects_before_touching_scratch(args):
+    """The no-alloc split converter validates every argument before it launches
+    the offset scan into its shared device array: these calls return an error
+    without any CUDA call (this container has no GPU, so a CUDA call would
+    report MXB_ERR_CUDA instead)."""
+    st = capi.status_of("mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit_noalloc", *args)
+    assert st in (1, 2), (st, capi.last_error())
+    assert "CUDA" not in capi.last_error()

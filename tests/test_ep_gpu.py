@@ -182,3 +182,42 @@ def test_moe_permute_mxfp4(cuda, rows, H, topk, wire):
     torch.cuda.synchronize()
     np.testing.assert_array_equal(oc.cpu().numpy(), oc_ref)
     np.testing.assert_array_equal(os_.cpu().numpy(), os_ref)
+
+
+# ------------------------------------------------------------------ bounded waits
+def test_p2p_wait_gives_up_and_reports(cuda):
+    """A cross-GPU wait whose peer never signals gives up after the configured
+    number of polls and is counted, leaving the context usable.  The "world" is
+    two ranks whose buffers are both this GPU's own buffer: rank 1 never runs,
+    so its flag stays 0 and both the count exchange and the barrier run out
+    (a short bounded wait on a flag that nothing sets; no peer memory, no fault)."""
+    import ctypes
+    L = capi.EpLayout()
+    total = ctypes.c_int64()
+    capi.call("mxb_ep_layout_init", 2, 0, 16, 512, 2, 4, ctypes.byref(L), ctypes.byref(total))
+    buf = torch.zeros(total.value, dtype=torch.uint8, device=cuda)
+    bases = torch.tensor([buf.data_ptr(), buf.data_ptr()], dtype=torch.int64, device=cuda)
+    counts = torch.zeros(2, dtype=torch.int32, device=cuda)
+    s = torch.cuda.current_stream().cuda_stream
+    lib = capi.load()
+    torch.cuda.synchronize()
+    lib.mxb_ep_reset_wait_timeouts()
+    try:
+        capi.call("mxb_ep_set_wait_polls", 2000)
+        capi.call("mxb_ep_p2p_counts", bases.data_ptr(), ctypes.byref(L), counts.data_ptr(), 0, 1, s)
+        capi.call("mxb_ep_p2p_barrier", bases.data_ptr(), ctypes.byref(L), 2, s)
+        torch.cuda.synchronize()
+        assert lib.mxb_ep_wait_timeouts() == 2
+        # the context is still usable and the own flag carries the last epoch
+        sig = buf[L.sig_off:L.sig_off + 8].view(torch.int32).cpu().tolist()
+        assert sig == [2, 0]
+        # a wait that is satisfied does not count: raise the peer's flag by hand
+        buf[L.sig_off + 4:L.sig_off + 8].view(torch.int32).fill_(3)
+        capi.call("mxb_ep_p2p_barrier", bases.data_ptr(), ctypes.byref(L), 3, s)
+        torch.cuda.synchronize()
+        assert lib.mxb_ep_wait_timeouts() == 2
+    finally:
+        capi.call("mxb_ep_set_wait_polls", 0)
+        torch.cuda.synchronize()
+        lib.mxb_ep_reset_wait_timeouts()
+    assert lib.mxb_ep_wait_timeouts() == 0

@@ -9,6 +9,7 @@ import pytest
 import torch
 
 import helpers as H
+from mxfp4_b200 import capi
 from mxfp4_b200 import synthetic as syn
 
 pytestmark = pytest.mark.gpu
@@ -411,3 +412,10 @@ def test_fp8_dequant_all_codes(cuda, orc):
     out = H.dequant_fp8(torch.from_numpy(q).view(torch.float8_e4m3fn).to(cuda),
                         torch.from_numpy(s).to(cuda))
     H.assert_bytes_equal(H.np_u16(out), orc.fp8_dequant_rows(q, s), "dequant")
+
+
+def test_no_pipeline_wait_gave_up(cuda):
+    """Every mbarrier wait of the kernels above (quantizers, column and split
+    converters) finished in time: the library-wide counter is still zero."""
+    torch.cuda.synchronize()
+    assert capi.wait_timeouts() == 0
