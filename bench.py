@@ -506,12 +506,9 @@ def _ops_config3(dev, sh, timeit, capi, syn):
     # colT-split: config 3's rows as 8 ragged expert segments (seeded sizes, not
     # multiples of 128, summing to M3), the grouped-GEMM wgrad operand; and the same
     # shares rounded to multiples of 128 (every output row 16-byte aligned)
-    gsz = torch.Generator().manual_seed(7)
-    wts = torch.rand(8, generator=gsz) + 0.5
     for name, q in (("mxfp4_to_fp8_colT_msplit8_config3", 1),
                     ("mxfp4_to_fp8_colT_msplit8x128_config3", 128)):
-        m_splits = ((wts / wts.sum() * M3 / q).floor() * q).to(torch.int64).tolist()
-        m_splits[-1] += M3 - sum(m_splits)
+        m_splits = syn.config3_splits(M3, 8, q)
         so, sco, acc, accs = [], [], 0, 0
         for m in m_splits:
             so.append(acc)

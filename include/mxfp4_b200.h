@@ -110,6 +110,30 @@ mxb_status mxb_quant_mxfp4_rowcol(const void* input, int64_t M, int64_t K, int64
                                   void* scales_col, void* scales_row_swizzled, float eps,
                                   float fp4_min, float fp4_max, mxb_stream_t stream);
 
+/* Shared-scale rule of a quantize call. */
+typedef enum {
+  /* The reference's rule: y_s = 2^ceil(log2(max(amax / 6, 1e-10)))
+   * (code/kernel/per_token_quant_mxfp4.cu:183-192). */
+  MXB_SCALE_REFERENCE = 0,
+  /* The OCP MX rule: 2^(floor(log2(max(amax, 1e-10))) - 2), the E2M1 emax
+   * being 2; a block whose amax is infinite gets the E8M0 NaN byte 0xFF.
+   * Differs from the reference rule on ~29% of N(0,1) blocks (by +1 in the
+   * reference's favour); no reference counterpart. */
+  MXB_SCALE_OCP = 1
+} mxb_scale_rule;
+
+/* One entry for the rowwise and/or columnwise quantize with a selectable
+ * scale rule (mxb_scale_rule; eps 1e-10 and clamp +-6, the reference API's
+ * configuration).  With codes_col and scales_col NULL it is the rowwise
+ * quantize of mxb_per_token_group_quant_fp4 (M any, ldx % 8 == 0), the
+ * swizzled copy of the row scales written if scales_row_swizzled is given;
+ * otherwise it is mxb_quant_mxfp4_rowcol (M % 32 == 0).  With
+ * MXB_SCALE_REFERENCE the bytes equal those entry points'. */
+mxb_status mxb_quantize_mxfp4(const void* input, int64_t M, int64_t K, int64_t ldx,
+                              void* codes_row, void* scales_row, void* codes_col,
+                              void* scales_col, void* scales_row_swizzled, int scale_rule,
+                              mxb_stream_t stream);
+
 /* mxb_quant_mxfp4_rowcol on HOST buffers (the end-to-end call for data in host
  * memory; pinned memory for full speed): x_host bf16 [M, K] -> codes_row_host
  * [M, K/2], scales_row_host [M, K/32], codes_col_host [K, M/2], scales_col_host
@@ -153,6 +177,27 @@ mxb_status mxb_per_token_Mxfp4ToBf16_dequant(const void* input, const void* inpu
  * output_s float [Kb/64, M] (M-contiguous, Transformer Engine GEMM_READY). */
 mxb_status mxb_per_token_Mxfp4ToFp8(const void* input, const void* input_s, int64_t M, int64_t Kb,
                                     void* output_q, void* output_s, mxb_stream_t stream);
+
+/* mxb_per_token_Mxfp4ToFp8 without the reference's 16-bit re-basing wrap:
+ * every element is its true value e2m1 * 2^(e - 127) divided by the group
+ * scale 2^(max e - 6 - 127), rounded to E4M3 (RNE, saturating), so zero codes
+ * stay zero where the reference writes +-448 and far-below-maximum blocks
+ * underflow to zero.  Same shapes and group scales.  No reference
+ * counterpart (an option of the rowwise converter, off by default). */
+mxb_status mxb_per_token_Mxfp4ToFp8_strict(const void* input, const void* input_s, int64_t M,
+                                           int64_t Kb, void* output_q, void* output_s,
+                                           mxb_stream_t stream);
+
+/* MXFP4 -> FP8 E4M3 with ONE FP32 scale per row: each row is dequantized as
+ * mxb_per_token_Mxfp4ToBf16_dequant does, then quantized per token as
+ * mxb_per_token_quant_fp8 does (amax = max(eps, max |x|), scale = amax/448,
+ * q = E4M3(clamp(x * 448/amax, +-448))), in one pass.  input uint8 [M, Kb]
+ * (Kb % 16 == 0), input_s uint8 [M, Kb/16], output_q fp8 [M, 2*Kb],
+ * output_s float [M].  No reference kernel: the per-row variant of the
+ * rowwise converter (the reference's groups are 1x128). */
+mxb_status mxb_per_token_Mxfp4ToFp8_rowscale(const void* input, const void* input_s, int64_t M,
+                                             int64_t Kb, void* output_q, void* output_s, float eps,
+                                             mxb_stream_t stream);
 
 /* Same operation under the name the reference binds at code/kernel/ops.cu:32
  * (omo_per_token_Mxfp4ToBf16ToFp8, whose source the reference does not ship). */

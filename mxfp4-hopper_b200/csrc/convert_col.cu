@@ -363,16 +363,18 @@ __device__ __forceinline__ uint32_t colT_scale_word(const uint8_t* scales, int64
 }
 
 // Stores row r's four E8M0 factors of a tile as float bit patterns (e << 23:
-// e = 0 reads 0, e = 255 reads Inf, as the reference's BF16 reading does; 1.0
-// past the tile's edges) into fac[q * 128 + r]; true if a factor is Inf.
-__device__ __forceinline__ bool colT_factors(uint32_t sc, const ColTTile& g, int r, uint32_t* fac) {
+// e = 0 reads 0, e = 255 reads Inf, as the reference's BF16 reading does)
+// into fac[q * 128 + r]; true if a factor is Inf.  colT_scale_word leaves the
+// bytes past the tile's edges 0, whose factor 0 meets only zero codes there
+// (the copy's zero fill, or the split path's masked rows), so the tile's
+// shape is not needed here.
+__device__ __forceinline__ bool colT_factors(uint32_t sc, int r, uint32_t* fac) {
   bool special = false;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const uint32_t e = (sc >> (8 * q)) & 0xFFu;
-    const bool in = r < g.rows && q * 32 < g.cols;
-    fac[q * 128 + r] = in ? e << 23 : 0x3F800000u;
-    special = special || (in && e == 255u);
+    fac[q * 128 + r] = e << 23;
+    special = special || e == 255u;
   }
   return special;
 }
@@ -620,7 +622,7 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
     mbar_arrive_expect_tx(&full[0], kColTCodeBytes);
     tma_load_2d(ctiles, &tmap, (int32_t)(g.col0 / 2), (int32_t)g.row_start, &full[0]);
   }
-  if (t < 128) special_next = colT_factors(colT_scale_word(scales, S, g, t), g, t, fac);
+  if (t < 128) special_next = colT_factors(colT_scale_word(scales, S, g, t), t, fac);
   __syncthreads();
 
   int issued = 1;  // code tiles requested so far (tile i uses stage i & 1)
@@ -734,6 +736,9 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
       col_qs[t] = qs;
       // NaN products are possible only with an Inf amax or an E8M0 byte of 255
       col_clamp[t] = (mb >= 0x7F800000u || tile_special) ? 1 : 0;
+      // tile i+1's factors into the other buffer (last read in tile i-1's step
+      // 1); the barrier below orders these stores before tile i+1's step 1
+      if (has_next) special_next = colT_factors(sc_next, t, fac + ((i + 1) & 1) * 512);
     }
     __syncthreads();
 
@@ -807,14 +812,13 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
     if (!has_next) return;
     // tile i+1 (on the split path rebuilt from its walk position, so that its
     // descriptor is not kept live through the tile: 128 registers with no
-    // spills) and its factors; that buffer was last read in tile i-1's step 1
+    // spills)
     w = wn;
     if constexpr (kSplit) {
       split_tile(w, N, sa, g);
     } else {
       g = gn;
     }
-    if (t < 128) special_next = colT_factors(sc_next, g, t, fac + ((i + 1) & 1) * 512);
   }
   // Left early (tile `issued - 2` or `issued - 1` never arrived): do not exit
   // while a requested copy may still land in this CTA's memory.

@@ -90,6 +90,36 @@ constexpr Fp8Lut make_fp8_lut(bool col) {
   return t;
 }
 
+// The strict rowwise table: the true value e2m1(n) * 2^(6 - d) of a nibble
+// re-based onto the group scale 2^(max_e - 6 - 127), rounded to E4M3 (RNE,
+// values below half the smallest subnormal become a signed zero), instead of
+// the reference's 16-bit re-basing, whose wrap turns zero codes (and tiny
+// codes far below the group maximum) into +-448.  No reference counterpart.
+constexpr Fp8Lut make_fp8_lut_strict() {
+  Fp8Lut t{};
+  for (uint32_t d = 0; d < 256; ++d) {
+    for (uint32_t n = 0; n < 16; ++n) {
+      const uint32_t em = n & 7u, sign = (n & 8u) << 4;
+      if (em == 0u) {
+        t.v[d][n] = (uint8_t)sign;
+        continue;
+      }
+      // e2m1 magnitude = (1 + f/2) * 2^E0: em 1 -> 0.5, 2 -> 1, 3 -> 1.5, 4 -> 2,
+      // 5 -> 3, 6 -> 4, 7 -> 6
+      const int E0 = em == 1u ? -1 : (int)(em >> 1) - 1;
+      const uint32_t half = (em >= 2u && (em & 1u)) ? 0x40u : 0u;
+      const int E = E0 + 6 - (int)d;
+      if (E + 127 < 1) {
+        t.v[d][n] = (uint8_t)sign;
+        continue;
+      }
+      const uint32_t bf = (sign << 8) | ((uint32_t)(E + 127) << 7) | half;
+      t.v[d][n] = lut_bf16_to_e4m3(bf);
+    }
+  }
+  return t;
+}
+
 // The col table ignores the nibble's sign bit (the reference masks bit 15 after
 // the subtraction), so entries n and n | 8 coincide and 8 entries suffice.
 constexpr bool col_lut_sign_free(const Fp8Lut& t) {

@@ -85,6 +85,43 @@ __device__ __forceinline__ void scale_fast(uint32_t mb, uint32_t& byte, uint32_t
   inv = (uint32_t)(127 - k) << 7;
 }
 
+// ---- OCP scale rule (MX specification v1.0: shared exponent
+// floor(log2(amax)) - emax(E2M1) with emax = 2), selectable instead of the
+// reference rule.  amax = max(1e-10, max |x|) as on the reference path, so an
+// all-zero block has exponent floor(log2(1e-10)) - 2 = -36 (byte 91).
+// Fast path: a finite BF16 amax pattern mb = 1.m * 2^(E - 127) gives
+// k = E - 129, and the 1e-10 floor is the clamp k >= -36.
+__device__ __forceinline__ void scale_fast_ocp(uint32_t mb, uint32_t& byte, uint32_t& inv) {
+  int k = (int)(mb >> 7) - 129;
+  k = k < -36 ? -36 : k;
+  byte = (uint32_t)(k + 127);
+  inv = (uint32_t)(127 - k) << 7;
+}
+// Generic path of the OCP rule (amax already floored at eps and NaN-free, as
+// fmaxf leaves it).  An infinite amax gives the E8M0 NaN byte 0xFF and inv = 0,
+// so finite elements encode as signed zeros and infinite ones saturate.
+__device__ __forceinline__ void scale_generic_ocp(float amax, float& inv, uint32_t& byte) {
+  const uint32_t e = (__float_as_uint(amax) >> 23) & 0xFFu;
+  if (e == 0xFFu) {
+    byte = 0xFFu;
+    inv = 0.0f;
+    return;
+  }
+  const int k = (int)e - 129;
+  byte = (uint32_t)(k + 127);
+  inv = __uint_as_float((uint32_t)(127 - k) << 23);
+}
+// The rule chosen at compile time: kOcp selects the OCP rule.
+template <bool kOcp>
+__device__ __forceinline__ void scale_fast_rule(uint32_t mb, uint32_t& byte, uint32_t& inv) {
+  if constexpr (kOcp) scale_fast_ocp(mb, byte, inv); else scale_fast(mb, byte, inv);
+}
+template <bool kOcp>
+__device__ __forceinline__ void scale_generic_rule(float amax, const QuantParams& p, float& inv,
+                                                   uint32_t& byte) {
+  if constexpr (kOcp) scale_generic_ocp(amax, inv, byte); else scale_generic(amax, p, inv, byte);
+}
+
 // Eight BF16 values times the BF16 power of two `inv` -> one word of eight
 // E2M1 codes (value i in nibble i).  Each product is formed by the sm_100
 // mixed-precision fma.rn.f32.bf16 (a * b + -0 in f32), which widens and scales
@@ -182,13 +219,13 @@ __device__ __forceinline__ void unpack8(const uint32_t* w, uint32_t (&f)[8]) {
 }
 
 // Quantizes one 32-element block held as 16 BF16 pairs in element order.
-template <bool kFast>
+template <bool kFast, bool kOcp = false>
 __device__ __forceinline__ void quant_block32(const uint32_t (&w)[16], const QuantParams& p,
                                               uint32_t (&out)[4], uint32_t& byte) {
   const uint32_t mb = max_abs_pairs(w);
   if (kFast && mb < 0x7F80u) {
     uint32_t inv;
-    scale_fast(mb, byte, inv);
+    scale_fast_rule<kOcp>(mb, byte, inv);
 #pragma unroll
     for (int i = 0; i < 4; ++i) out[i] = encode8_pairs(&w[4 * i], inv);
   } else {
@@ -201,7 +238,7 @@ __device__ __forceinline__ void quant_block32(const uint32_t (&w)[16], const Qua
       for (int j = 0; j < 8; ++j) fa[8 * i + j] = f[j];
     }
     float inv;
-    scale_generic(amax_generic(fa, p.eps), p, inv, byte);
+    scale_generic_rule<kOcp>(amax_generic(fa, p.eps), p, inv, byte);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint32_t f[8];

@@ -54,7 +54,7 @@ __device__ __forceinline__ int64_t swizzle_offset(int64_t r, int64_t c, int64_t 
 // codes are never re-read from HBM.
 __device__ const Fp8Lut g_lut_fused = make_fp8_lut(false);
 
-template <bool kFast, bool kFp8>
+template <bool kFast, bool kFp8, bool kOcp = false>
 __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __restrict__ x,
                                                          int64_t M, int64_t K, int64_t ldx,
                                                          uint8_t* __restrict__ codes,
@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __
     uint32_t byte, out[2];
     if (kFast && mb < 0x7F80u) {
       uint32_t inv;
-      scale_fast(mb, byte, inv);
+      scale_fast_rule<kOcp>(mb, byte, inv);
       out[0] = encode8_pairs(&w[0], inv);
       out[1] = encode8_pairs(&w[4], inv);
     } else {
@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __
       float am = fmaxf(amax_generic(f0, p.eps), amax_generic(f1, p.eps));
       am = fmaxf(am, __shfl_xor_sync(pair_mask, am, 1));
       float inv;
-      scale_generic(am, p, inv, byte);
+      scale_generic_rule<kOcp>(am, p, inv, byte);
       out[0] = encode8_generic(f0, inv, p);
       out[1] = encode8_generic(f1, inv, p);
     }
@@ -158,7 +158,7 @@ __device__ __forceinline__ uint32_t sw64(uint32_t r, uint32_t c) {
   return r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
 }
 
-template <bool kFast, bool kRows>
+template <bool kFast, bool kRows, bool kOcp = false>
 __global__ void __launch_bounds__(kRowColThreads, 2) quant_rowcol_kernel(
     const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__ CUtensorMap tmap_row,
     const __grid_constant__ CUtensorMap tmap_col, int64_t M, int64_t K,
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(kRowColThreads, 2) quant_rowcol_kernel(
           w[4 * j] = v.x; w[4 * j + 1] = v.y; w[4 * j + 2] = v.z; w[4 * j + 3] = v.w;
         }
         uint32_t out[4], byte;
-        quant_block32<kFast>(w, p, out, byte);  // out[j] encodes chunk (j + rsub) & 3
+        quant_block32<kFast, kOcp>(w, p, out, byte);  // out[j] encodes chunk (j + rsub) & 3
         rotate4(out, rsub);
         *reinterpret_cast<uint4*>(o_row + sw64(r, g)) = make_uint4(out[0], out[1], out[2], out[3]);
         s_row[r * 4 + g] = (uint8_t)byte;
@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(kRowColThreads, 2) quant_rowcol_kernel(
         uint32_t out[4], byte;
         if (kFast && mb < 0x7F80u) {
           uint32_t inv;
-          scale_fast(mb, byte, inv);
+          scale_fast_rule<kOcp>(mb, byte, inv);
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             out[q] = h ? encode8_half<true>(&w[8 * q], inv) : encode8_half<false>(&w[8 * q], inv);
@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(kRowColThreads, 2) quant_rowcol_kernel(
 #pragma unroll
           for (int r = 0; r < 32; ++r) fa[r] = h ? (w[r] & 0xFFFF0000u) : (w[r] << 16);
           float inv;
-          scale_generic(amax_generic(fa, p.eps), p, inv, byte);
+          scale_generic_rule<kOcp>(amax_generic(fa, p.eps), p, inv, byte);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t f[8];
@@ -443,14 +443,19 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const __nv_bfloat16* 
 template <bool kFp8>
 void launch_quant_rows(bool fast, const void* input, int64_t M, int64_t K, int64_t ldx,
                        void* output_q, void* output_s, const QuantParams& p, void* fp8, void* fp8_s,
-                       mxb_stream_t stream) {
+                       mxb_stream_t stream, bool ocp = false) {
   const void* kern = fast ? (const void*)quant_rows_kernel<true, kFp8>
                           : (const void*)quant_rows_kernel<false, kFp8>;
+  if (ocp) kern = (const void*)quant_rows_kernel<true, kFp8, true>;
   const int64_t halves = M * (K / 32) * 2;
   const int64_t want = cdiv(halves, 256);
   const int64_t cap = (int64_t)persistent_ctas(kern, 256, 0) * 4;
   const int grid = (int)(want < cap ? want : cap);
-  if (fast)
+  if (ocp)
+    quant_rows_kernel<true, kFp8, true><<<grid, 256, 0, to_cuda(stream)>>>(
+        (const __nv_bfloat16*)input, M, K, ldx, (uint8_t*)output_q, (uint8_t*)output_s, p,
+        (uint8_t*)fp8, (float*)fp8_s);
+  else if (fast)
     quant_rows_kernel<true, kFp8><<<grid, 256, 0, to_cuda(stream)>>>(
         (const __nv_bfloat16*)input, M, K, ldx, (uint8_t*)output_q, (uint8_t*)output_s, p,
         (uint8_t*)fp8, (float*)fp8_s);
@@ -545,11 +550,12 @@ extern "C" mxb_status mxb_swiglu_quant_mxfp4(const void* input, int64_t M, int64
   return launch_status("swiglu_quant");
 }
 
-extern "C" mxb_status mxb_quant_mxfp4_rowcol(const void* input, int64_t M, int64_t K, int64_t ldx,
-                                             void* codes_row, void* scales_row, void* codes_col,
-                                             void* scales_col, void* scales_row_swizzled,
-                                             float eps, float fp4_min, float fp4_max,
-                                             mxb_stream_t stream) {
+// The fused row + column quantize behind mxb_quant_mxfp4_rowcol and
+// mxb_quantize_mxfp4 (ocp: the OCP scale rule, default parameters only).
+static mxb_status quant_rowcol_impl(const void* input, int64_t M, int64_t K, int64_t ldx,
+                                    void* codes_row, void* scales_row, void* codes_col,
+                                    void* scales_col, void* scales_row_swizzled, float eps,
+                                    float fp4_min, float fp4_max, bool ocp, mxb_stream_t stream) {
   MXB_REQUIRE(M >= 0 && K >= 0 && M % 32 == 0 && K % 32 == 0, MXB_ERR_INVALID_ARGUMENT,
               "quant_rowcol: need M %% 32 == 0 and K %% 32 == 0 (M=%lld K=%lld)", (long long)M,
               (long long)K);
@@ -594,10 +600,12 @@ extern "C" mxb_status mxb_quant_mxfp4_rowcol(const void* input, int64_t M, int64
                         uint8_t*, uint8_t*, uint8_t*, QuantParams, int, int);
   Kern kern = codes_row ? (fast ? quant_rowcol_kernel<true, true> : quant_rowcol_kernel<false, true>)
                         : (fast ? quant_rowcol_kernel<true, false> : quant_rowcol_kernel<false, false>);
+  if (ocp) kern = codes_row ? quant_rowcol_kernel<true, true, true> : quant_rowcol_kernel<true, false, true>;
   static const bool attr_ok = [] {
     bool ok = true;
     for (Kern k : {quant_rowcol_kernel<true, true>, quant_rowcol_kernel<false, true>,
-                   quant_rowcol_kernel<true, false>, quant_rowcol_kernel<false, false>})
+                   quant_rowcol_kernel<true, false>, quant_rowcol_kernel<false, false>,
+                   quant_rowcol_kernel<true, true, true>, quant_rowcol_kernel<true, false, true>})
       ok &= cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kRowColSmem) == cudaSuccess;
     return ok;
@@ -609,6 +617,45 @@ extern "C" mxb_status mxb_quant_mxfp4_rowcol(const void* input, int64_t M, int64
   kern<<<grid, kRowColThreads, kRowColSmem, s>>>(tm_in, tm_row, tm_col, M, K, sr, sc, sw, p,
                                                  (int)col_tiles, (int)tiles);
   return launch_status("quant_rowcol");
+}
+
+extern "C" mxb_status mxb_quant_mxfp4_rowcol(const void* input, int64_t M, int64_t K, int64_t ldx,
+                                             void* codes_row, void* scales_row, void* codes_col,
+                                             void* scales_col, void* scales_row_swizzled,
+                                             float eps, float fp4_min, float fp4_max,
+                                             mxb_stream_t stream) {
+  return quant_rowcol_impl(input, M, K, ldx, codes_row, scales_row, codes_col, scales_col,
+                           scales_row_swizzled, eps, fp4_min, fp4_max, false, stream);
+}
+
+extern "C" mxb_status mxb_quantize_mxfp4(const void* input, int64_t M, int64_t K, int64_t ldx,
+                                         void* codes_row, void* scales_row, void* codes_col,
+                                         void* scales_col, void* scales_row_swizzled,
+                                         int scale_rule, mxb_stream_t stream) {
+  MXB_REQUIRE(scale_rule == MXB_SCALE_REFERENCE || scale_rule == MXB_SCALE_OCP,
+              MXB_ERR_INVALID_ARGUMENT, "quantize_mxfp4: unknown scale rule %d", scale_rule);
+  const bool ocp = scale_rule == MXB_SCALE_OCP;
+  const float eps = 1e-10f, lo = -6.0f, hi = 6.0f;
+  if (codes_col || scales_col)
+    return quant_rowcol_impl(input, M, K, ldx, codes_row, scales_row, codes_col, scales_col,
+                             scales_row_swizzled, eps, lo, hi, ocp, stream);
+  // rowwise only
+  MXB_REQUIRE(M >= 0 && K >= 0 && K % 32 == 0, MXB_ERR_INVALID_ARGUMENT,
+              "quantize_mxfp4: need M >= 0 and K %% 32 == 0 (M=%lld K=%lld)", (long long)M,
+              (long long)K);
+  MXB_REQUIRE(ldx >= K && ldx % 8 == 0, MXB_ERR_MISALIGNED,
+              "quantize_mxfp4: row pitch must be >= K and a multiple of 8 elements");
+  if (M == 0 || K == 0) return MXB_OK;
+  MXB_REQUIRE(input && codes_row && scales_row, MXB_ERR_INVALID_ARGUMENT,
+              "quantize_mxfp4: null pointer (a rowwise call needs codes_row and scales_row)");
+  MXB_REQUIRE(aligned(input, 16) && aligned(codes_row, 8), MXB_ERR_MISALIGNED,
+              "quantize_mxfp4: input must be 16-byte and codes_row 8-byte aligned");
+  const QuantParams p{eps, lo, hi};
+  launch_quant_rows<false>(true, input, M, K, ldx, codes_row, scales_row, p, nullptr, nullptr,
+                           stream, ocp);
+  mxb_status st = launch_status("quantize_mxfp4");
+  if (st != MXB_OK || !scales_row_swizzled) return st;
+  return mxb_swizzle_scales(scales_row, M, K / 32, scales_row_swizzled, stream);
 }
 
 extern "C" unsigned int mxb_wait_timeouts(void) { return sum_wait_timeouts(false); }

@@ -32,6 +32,9 @@ SIGNATURES = {
     "mxb_per_token_Mxfp4ToBf16_dequant": [_P, _P, _I64, _I64, _P, _P],
     "mxb_per_token_Mxfp4ToFp8": [_P, _P, _I64, _I64, _P, _P, _P],
     "mxb_per_token_Mxfp4ToBf16ToFp8": [_P, _P, _I64, _I64, _P, _P, _P],
+    "mxb_per_token_Mxfp4ToFp8_strict": [_P, _P, _I64, _I64, _P, _P, _P],
+    "mxb_per_token_Mxfp4ToFp8_rowscale": [_P, _P, _I64, _I64, _P, _P, _F, _P],
+    "mxb_quantize_mxfp4": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I, _P],
     "mxb_per_token_Mxfp4ToFp8_col": [_P, _P, _I64, _I64, _P, _P, _P],
     "mxb_per_token_Mxfp4RowToBf16ToFp8Col": [_P, _P, _I64, _I64, _P, _P, _F, _P],
     "mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit": [_P, _P, _I64, _I64, _P, _P, _P, _P, _P,

@@ -51,6 +51,16 @@ def config3(rows: int = 16384, code_bytes: int = 8192, seed: int = 2, lo: int = 
     return codes, scales
 
 
+def config3_splits(rows: int = 16384, segments: int = 8, multiple: int = 1, seed: int = 7):
+    """Seeded expert-segment sizes for the split converter (the grouped-GEMM
+    wgrad operand): `segments` shares of `rows`, each a multiple of `multiple`
+    (1: ragged), summing to rows."""
+    wts = torch.rand(segments, generator=_gen(seed)) + 0.5
+    m = ((wts / wts.sum() * rows / multiple).floor() * multiple).to(torch.int64).tolist()
+    m[-1] += rows - sum(m)
+    return m
+
+
 def config4(rows: int = 32768, cols: int = 7168, seed: int = 3) -> torch.Tensor:
     g = _gen(seed)
     x = torch.randn(rows, cols, generator=g, dtype=torch.float32)

@@ -133,29 +133,53 @@ static inline void scale_rule_ref(float amax, float fp4_max, float* y_s, uint8_t
   *byte = (uint8_t)(k + 127);
 }
 
+/* The OCP MX shared-exponent rule, a selectable alternative to the reference
+ * rule (no reference counterpart; OCP Microscaling Formats spec v1.0, section
+ * 6.3): X = 2^(floor(log2(amax)) - emax) with emax = 2 for E2M1, amax floored
+ * at eps = 1e-10 as on the reference path.  An infinite amax gives the E8M0
+ * NaN byte 0xFF and a zero multiplier.  Returns the multiplier 1/X. */
+static inline float scale_rule_ocp(float amax, uint8_t* byte) {
+  uint32_t e = (bits_from_f(amax) >> 23) & 0xFFu;
+  if (e == 0xFFu) { *byte = 0xFF; return 0.0f; }
+  int k = (int)e - 127 - 2; /* amax >= 1e-10 is normal */
+  *byte = (uint8_t)(k + 127);
+  return ldexpf(1.0f, -k);
+}
+
+/* One 1x32 block (values v[0..31]) under the reference rule (ocp = 0) or the
+ * OCP rule (ocp = 1, with the reference API's eps and clamp). */
+static inline void quant_block(const float* v, float eps, float fp4_min, float fp4_max, int ocp,
+                               uint8_t* cb, uint8_t* sb) {
+  float amax = eps;
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  float inv;
+  if (ocp) {
+    inv = scale_rule_ocp(amax, sb);
+  } else {
+    float y_s;
+    scale_rule_ref(amax, fp4_max, &y_s, sb);
+    inv = 1.0f / y_s;
+  }
+  for (int i = 0; i < 16; ++i) {
+    float q0 = fminf(fmaxf(v[2 * i] * inv, fp4_min), fp4_max);
+    float q1 = fminf(fmaxf(v[2 * i + 1] * inv, fp4_min), fp4_max);
+    cb[i] = (uint8_t)((e2m1_encode_ref(q0) & 0x0F) | ((e2m1_encode_ref(q1) & 0x0F) << 4));
+  }
+}
+
 /* ----------------------------------------------------------- Q-row (C1) */
-/* Rowwise BF16 -> MXFP4 quantize, 1x32 blocks (per_token_quant_mxfp4.cu:121-266).
+/* Rowwise BF16 -> MXFP4 quantize, 1x32 blocks (per_token_quant_mxfp4.cu:121-266:
+ * amax :151,171-178, scale :183-196, clamp and encode :200-256).
  * x: [M, K] bf16 bits, row stride ldx elements; codes: [M, K/2]; scales: [M, K/32]. */
-void orc_quant_mxfp4_rows(const uint16_t* x, int64_t M, int64_t K, int64_t ldx, float eps,
-                          float fp4_min, float fp4_max, uint8_t* codes, uint8_t* scales) {
+static void quant_rows(const uint16_t* x, int64_t M, int64_t K, int64_t ldx, float eps,
+                       float fp4_min, float fp4_max, int ocp, uint8_t* codes, uint8_t* scales) {
   const int64_t G = K / 32;
 #pragma omp parallel for schedule(static)
   for (int64_t r = 0; r < M; ++r) {
     for (int64_t g = 0; g < G; ++g) {
-      const uint16_t* xb = x + r * ldx + g * 32;
-      float amax = eps;
-      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(bf16_to_f(xb[i])));
-      float y_s;
-      uint8_t sb;
-      scale_rule_ref(amax, fp4_max, &y_s, &sb);
-      scales[r * G + g] = sb;
-      const float inv = 1.0f / y_s;
-      uint8_t* cb = codes + r * (K / 2) + g * 16;
-      for (int i = 0; i < 16; ++i) {
-        float q0 = fminf(fmaxf(bf16_to_f(xb[2 * i]) * inv, fp4_min), fp4_max);
-        float q1 = fminf(fmaxf(bf16_to_f(xb[2 * i + 1]) * inv, fp4_min), fp4_max);
-        cb[i] = (uint8_t)((e2m1_encode_ref(q0) & 0x0F) | ((e2m1_encode_ref(q1) & 0x0F) << 4));
-      }
+      float v[32];
+      for (int i = 0; i < 32; ++i) v[i] = bf16_to_f(x[r * ldx + g * 32 + i]);
+      quant_block(v, eps, fp4_min, fp4_max, ocp, codes + r * (K / 2) + g * 16, scales + r * G + g);
     }
   }
 }
@@ -163,31 +187,36 @@ void orc_quant_mxfp4_rows(const uint16_t* x, int64_t M, int64_t K, int64_t ldx, 
 /* Columnwise quantize: the reference applies Q-row to tensor.T.contiguous()
  * (transformer_engine-2.8.diff:1465-1466), so a block is 32 consecutive rows
  * of one column.  codes_t: [K, M/2]; scales_t: [K, M/32]. */
-void orc_quant_mxfp4_cols(const uint16_t* x, int64_t M, int64_t K, int64_t ldx, float eps,
-                          float fp4_min, float fp4_max, uint8_t* codes_t, uint8_t* scales_t) {
+static void quant_cols(const uint16_t* x, int64_t M, int64_t K, int64_t ldx, float eps,
+                       float fp4_min, float fp4_max, int ocp, uint8_t* codes_t, uint8_t* scales_t) {
   const int64_t G = M / 32;
 #pragma omp parallel for schedule(static)
   for (int64_t c = 0; c < K; ++c) {
     for (int64_t g = 0; g < G; ++g) {
       float v[32];
-      float amax = eps;
-      for (int i = 0; i < 32; ++i) {
-        v[i] = bf16_to_f(x[(g * 32 + i) * ldx + c]);
-        amax = fmaxf(amax, fabsf(v[i]));
-      }
-      float y_s;
-      uint8_t sb;
-      scale_rule_ref(amax, fp4_max, &y_s, &sb);
-      scales_t[c * G + g] = sb;
-      const float inv = 1.0f / y_s;
-      uint8_t* cb = codes_t + c * (M / 2) + g * 16;
-      for (int i = 0; i < 16; ++i) {
-        float q0 = fminf(fmaxf(v[2 * i] * inv, fp4_min), fp4_max);
-        float q1 = fminf(fmaxf(v[2 * i + 1] * inv, fp4_min), fp4_max);
-        cb[i] = (uint8_t)((e2m1_encode_ref(q0) & 0x0F) | ((e2m1_encode_ref(q1) & 0x0F) << 4));
-      }
+      for (int i = 0; i < 32; ++i) v[i] = bf16_to_f(x[(g * 32 + i) * ldx + c]);
+      quant_block(v, eps, fp4_min, fp4_max, ocp, codes_t + c * (M / 2) + g * 16,
+                  scales_t + c * G + g);
     }
   }
+}
+
+void orc_quant_mxfp4_rows(const uint16_t* x, int64_t M, int64_t K, int64_t ldx, float eps,
+                          float fp4_min, float fp4_max, uint8_t* codes, uint8_t* scales) {
+  quant_rows(x, M, K, ldx, eps, fp4_min, fp4_max, 0, codes, scales);
+}
+void orc_quant_mxfp4_cols(const uint16_t* x, int64_t M, int64_t K, int64_t ldx, float eps,
+                          float fp4_min, float fp4_max, uint8_t* codes_t, uint8_t* scales_t) {
+  quant_cols(x, M, K, ldx, eps, fp4_min, fp4_max, 0, codes_t, scales_t);
+}
+/* The same two under the OCP scale rule (eps 1e-10, clamp +-6). */
+void orc_quant_mxfp4_rows_ocp(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
+                              uint8_t* codes, uint8_t* scales) {
+  quant_rows(x, M, K, ldx, 1e-10f, -6.0f, 6.0f, 1, codes, scales);
+}
+void orc_quant_mxfp4_cols_ocp(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
+                              uint8_t* codes_t, uint8_t* scales_t) {
+  quant_cols(x, M, K, ldx, 1e-10f, -6.0f, 6.0f, 1, codes_t, scales_t);
 }
 
 /* Swizzled scale layout used by tcgen05 block-scaled MMA and cuBLAS
@@ -262,6 +291,35 @@ void orc_mxfp4_to_fp8_rows(const uint8_t* codes, const uint8_t* scales, int64_t 
         for (int b = 0; b < 16; ++b) {
           ob[2 * b] = fp8_from_rebased_row(cb[b] & 0xFu, adj);
           ob[2 * b + 1] = fp8_from_rebased_row(cb[b] >> 4, adj);
+        }
+      }
+    }
+  }
+}
+
+/* The rowwise convert without the re-basing wrap (no reference counterpart):
+ * the same group scale, each element its true value e2m1 * 2^(e - g - 127)
+ * with g = max e - 6, rounded to E4M3 (RNE, saturating; underflow gives a
+ * signed zero). */
+void orc_mxfp4_to_fp8_rows_strict(const uint8_t* codes, const uint8_t* scales, int64_t M,
+                                  int64_t Kb, uint8_t* out, float* scales_out) {
+  static const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  const int64_t S = Kb / 16, NG = Kb / 64;
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < M; ++r) {
+    for (int64_t g = 0; g < NG; ++g) {
+      const uint8_t* sp = scales + r * S + g * 4;
+      int mx = sp[0];
+      for (int j = 1; j < 4; ++j) mx = sp[j] > mx ? sp[j] : mx;
+      scales_out[g * M + r] = f_from_bits((uint32_t)(uint8_t)(mx - 6) << 23);
+      for (int j = 0; j < 4; ++j) {
+        const int shift = 6 - (mx - (int)sp[j]); /* <= 6 */
+        const uint8_t* cb = codes + r * Kb + g * 64 + j * 16;
+        uint8_t* ob = out + r * 2 * Kb + g * 128 + j * 32;
+        for (int b = 0; b < 32; ++b) {
+          unsigned nib = (b & 1) ? (cb[b / 2] >> 4) : (cb[b / 2] & 0xFu);
+          float v = ldexpf(mag[nib & 7u], shift);
+          ob[b] = orc_f32_to_e4m3((nib & 8u) ? -v : v);
         }
       }
     }

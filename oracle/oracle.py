@@ -44,6 +44,9 @@ def lib():
         sig = {
             "orc_quant_mxfp4_rows": [_P, _I64, _I64, _I64, _F, _F, _F, _P, _P],
             "orc_quant_mxfp4_cols": [_P, _I64, _I64, _I64, _F, _F, _F, _P, _P],
+            "orc_quant_mxfp4_rows_ocp": [_P, _I64, _I64, _I64, _P, _P],
+            "orc_quant_mxfp4_cols_ocp": [_P, _I64, _I64, _I64, _P, _P],
+            "orc_mxfp4_to_fp8_rows_strict": [_P, _P, _I64, _I64, _P, _P],
             "orc_swizzle_scales": [_P, _I64, _I64, _P],
             "orc_dequant_bf16": [_P, _P, _I64, _I64, _P],
             "orc_mxfp4_to_fp8_rows": [_P, _P, _I64, _I64, _P, _P],
@@ -81,23 +84,30 @@ def num_threads() -> int:
 
 
 # ---------------------------------------------------------------- quantize
-def quant_rows(x_bf16: np.ndarray, eps=1e-10, fp4_min=-6.0, fp4_max=6.0):
-    """Q-row, per_token_quant_mxfp4.cu:121-266 -> (codes [M,K/2], scales [M,K/32])."""
+def quant_rows(x_bf16: np.ndarray, eps=1e-10, fp4_min=-6.0, fp4_max=6.0, rule="reference"):
+    """Q-row, per_token_quant_mxfp4.cu:121-266 -> (codes [M,K/2], scales [M,K/32]).
+    rule="ocp": the OCP MX scale rule instead (default eps and clamp only)."""
     x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
     M, K = x.shape
     codes = np.empty((M, K // 2), np.uint8)
     scales = np.empty((M, K // 32), np.uint8)
-    lib().orc_quant_mxfp4_rows(_p(x), M, K, K, eps, fp4_min, fp4_max, _p(codes), _p(scales))
+    if rule == "ocp":
+        lib().orc_quant_mxfp4_rows_ocp(_p(x), M, K, K, _p(codes), _p(scales))
+    else:
+        lib().orc_quant_mxfp4_rows(_p(x), M, K, K, eps, fp4_min, fp4_max, _p(codes), _p(scales))
     return codes, scales
 
 
-def quant_cols(x_bf16: np.ndarray, eps=1e-10, fp4_min=-6.0, fp4_max=6.0):
+def quant_cols(x_bf16: np.ndarray, eps=1e-10, fp4_min=-6.0, fp4_max=6.0, rule="reference"):
     """Q-col: Q-row of x.T (transformer_engine-2.8.diff:1465-1466) -> ([K,M/2], [K,M/32])."""
     x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
     M, K = x.shape
     codes = np.empty((K, M // 2), np.uint8)
     scales = np.empty((K, M // 32), np.uint8)
-    lib().orc_quant_mxfp4_cols(_p(x), M, K, K, eps, fp4_min, fp4_max, _p(codes), _p(scales))
+    if rule == "ocp":
+        lib().orc_quant_mxfp4_cols_ocp(_p(x), M, K, K, _p(codes), _p(scales))
+    else:
+        lib().orc_quant_mxfp4_cols(_p(x), M, K, K, eps, fp4_min, fp4_max, _p(codes), _p(scales))
     return codes, scales
 
 
@@ -130,6 +140,24 @@ def mxfp4_to_fp8_rows(codes: np.ndarray, scales: np.ndarray):
     so = np.empty((Kb // 64, M), np.float32)
     lib().orc_mxfp4_to_fp8_rows(_p(c), _p(s), M, Kb, _p(out), _p(so))
     return out, so
+
+
+def mxfp4_to_fp8_rows_strict(codes: np.ndarray, scales: np.ndarray):
+    """Rowwise FP8 convert without the re-basing wrap (true values; no reference
+    counterpart) -> (fp8 [M,2Kb], f32 scales [Kb/64, M])."""
+    c = np.ascontiguousarray(codes, dtype=np.uint8)
+    s = np.ascontiguousarray(scales, dtype=np.uint8)
+    M, Kb = c.shape
+    out = np.empty((M, 2 * Kb), np.uint8)
+    so = np.empty((Kb // 64, M), np.float32)
+    lib().orc_mxfp4_to_fp8_rows_strict(_p(c), _p(s), M, Kb, _p(out), _p(so))
+    return out, so
+
+
+def mxfp4_to_fp8_rowscale(codes: np.ndarray, scales: np.ndarray, eps=1e-10):
+    """MXFP4 -> FP8 with one FP32 scale per row: DQ-bf16 then the per-token FP8
+    quantize (parity unpinned: no reference kernel) -> (fp8 [M,2Kb], f32 [M])."""
+    return fp8_quant_rows(dequant_bf16(codes, scales), eps)
 
 
 def mxfp4_to_fp8_cols(codes: np.ndarray, scales: np.ndarray):

@@ -80,6 +80,32 @@ def quant_rowcol(x, rows=True, swz=False, eps=1e-10, fmin=-6.0, fmax=6.0):
     return cr, sr, cc, sc, sw
 
 
+def quantize(x, rows=True, cols=False, swz=False, rule=0):
+    """mxb_quantize_mxfp4: rowwise and/or columnwise with a scale rule
+    (0 reference, 1 OCP)."""
+    M, K = x.shape
+    dev = x.device
+    cr = torch.empty(M, K // 2, dtype=torch.uint8, device=dev) if rows else None
+    sr = torch.empty(M, K // 32, dtype=torch.uint8, device=dev) if rows else None
+    cc = torch.empty(K, M // 2, dtype=torch.uint8, device=dev) if cols else None
+    sc = torch.empty(K, M // 32, dtype=torch.uint8, device=dev) if cols else None
+    sw = torch.empty((M + 127) // 128 * 128, (K // 32 + 3) // 4 * 4, dtype=torch.uint8,
+                     device=dev) if swz else None
+    capi.call("mxb_quantize_mxfp4", dp(x), M, K, K, dp(cr), dp(sr), dp(cc), dp(sc), dp(sw), rule,
+              stream())
+    return cr, sr, cc, sc, sw
+
+
+def to_fp8_rowscale(codes, scales, eps=1e-10):
+    """MXFP4 -> FP8 with one FP32 scale per row."""
+    M, Kb = codes.shape
+    q = torch.empty(M, 2 * Kb, dtype=torch.float8_e4m3fn, device=codes.device)
+    s = torch.empty(M, dtype=torch.float32, device=codes.device)
+    capi.call("mxb_per_token_Mxfp4ToFp8_rowscale", dp(codes), dp(scales), M, Kb, dp(q), dp(s), eps,
+              stream())
+    return q, s
+
+
 def dequant_bf16(codes, scales):
     M, Kb = codes.shape
     out = torch.empty(M, 2 * Kb, dtype=torch.bfloat16, device=codes.device)

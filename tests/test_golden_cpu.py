@@ -74,7 +74,9 @@ def test_fp8_colT_vs_reference_where_stable(orc, gold):
     c, s = syn.config3(256, 128, seed=22, lo=117, hi=137)
     q, so = orc.mxfp4_to_fp8_colT(c.numpy(), s.numpy())
     mq, ms = gold["fp8_colT_q_stable"], gold["fp8_colT_s_stable"]
-    assert mq.mean() > 0.5
+    # 96.7% of the FP8 bytes and 95.7% of the scales were identical over the
+    # reference's 8 runs when the fixture was made
+    assert mq.mean() > 0.95 and ms.mean() > 0.94
     assert np.array_equal(q[mq], gold["fp8_colT_q"][mq])
     so8 = _u8(so).reshape(so.shape[0], -1)
     assert np.array_equal(so8[ms], gold["fp8_colT_s"][ms])

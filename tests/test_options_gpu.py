@@ -1,0 +1,158 @@
+"""The options of the path that are off by default, through the C ABI, against
+the oracle: the OCP scale rule of the quantizer (BASELINE config 1 words its
+scale as floor(log2 amax) - 2), the strict rowwise FP8 convert (true zeros
+instead of the reference's +-448 wrap) and the per-row-scale FP8 convert.
+None has a reference kernel; the oracle functions state each rule."""
+import numpy as np
+import pytest
+import torch
+
+import helpers as H
+from mxfp4_b200 import synthetic as syn
+from test_parity_gpu import encode_kat_input, scale_kat_input, special_block_input
+
+pytestmark = pytest.mark.gpu
+
+RULES = {"reference": 0, "ocp": 1}
+
+
+def _dev(bits, cuda):
+    return H.bf16_from_bits(bits).to(cuda)
+
+
+# ------------------------------------------------------------ scale rule
+@pytest.mark.parametrize("rule", ["reference", "ocp"])
+def test_config1_under_both_rules(cuda, orc, rule):
+    """BASELINE config 1 ([4096, 4096], N(0,1) with 0.1% x100 outliers) quantized
+    rowwise and dequantized, under each rule; the two rules differ on ~29% of
+    blocks, always by one binade in the reference rule's favour."""
+    x = syn.config1(4096, 4096, seed=0)
+    xb = syn.bf16_bits(x)
+    cr, sr, _, _, _ = H.quantize(x.to(cuda), rule=RULES[rule])
+    rq, rs = orc.quant_rows(xb, rule=rule)
+    H.assert_bytes_equal(H.np_u8(sr), rs, "scales")
+    H.assert_bytes_equal(H.np_u8(cr), rq, "codes")
+    out = H.dequant_bf16(cr, sr)
+    H.assert_bytes_equal(H.np_u16(out), orc.dequant_bf16(rq, rs), "round trip")
+    if rule == "ocp":
+        _, ref_s = orc.quant_rows(xb)
+        d = ref_s.astype(np.int16) - rs.astype(np.int16)
+        assert set(np.unique(d).tolist()) <= {0, 1}
+        assert 0.2 < (d != 0).mean() < 0.4
+    else:  # the reference rule through the new entry equals the reference entry
+        q2, s2 = H.quant_rows(x.to(cuda))
+        assert torch.equal(q2, cr) and torch.equal(s2, sr)
+
+
+@pytest.mark.parametrize("kind", ["special", "scale_kat", "encode_kat"])
+def test_ocp_rows_edge_values(cuda, orc, kind):
+    xb = {"special": special_block_input, "scale_kat": scale_kat_input,
+          "encode_kat": encode_kat_input}[kind]()
+    cr, sr, _, _, _ = H.quantize(_dev(xb, cuda), rule=1)
+    rq, rs = orc.quant_rows(xb, rule="ocp")
+    H.assert_bytes_equal(H.np_u8(sr), rs, "scales")
+    H.assert_bytes_equal(H.np_u8(cr), rq, "codes")
+
+
+@pytest.mark.parametrize("shape", [(256, 512), (16384, 8192)])
+def test_ocp_rowcol(cuda, orc, shape):
+    """Row + column outputs in one pass under the OCP rule, with the swizzled
+    row scales; config 2's full shape included."""
+    x = syn.config2(*shape, seed=1)
+    xb = syn.bf16_bits(x)
+    if shape[0] <= 256:
+        xb[:9, :64] = special_block_input()
+    cr, sr, cc, sc, sw = H.quantize(_dev(xb, cuda), cols=True, swz=True, rule=1)
+    rq, rs = orc.quant_rows(xb, rule="ocp")
+    cq, cs = orc.quant_cols(xb, rule="ocp")
+    H.assert_bytes_equal(H.np_u8(sr), rs, "row scales")
+    H.assert_bytes_equal(H.np_u8(cr), rq, "row codes")
+    H.assert_bytes_equal(H.np_u8(sc), cs, "col scales")
+    H.assert_bytes_equal(H.np_u8(cc), cq, "col codes")
+    H.assert_bytes_equal(H.np_u8(sw), orc.swizzle_scales(rs), "swizzled")
+
+
+def test_rowwise_only_with_swizzle(cuda, orc):
+    x = syn.config1(300, 1024, seed=3)
+    xb = syn.bf16_bits(x)
+    cr, sr, _, _, sw = H.quantize(x.to(cuda), swz=True, rule=0)
+    rq, rs = orc.quant_rows(xb)
+    H.assert_bytes_equal(H.np_u8(cr), rq, "codes")
+    H.assert_bytes_equal(H.np_u8(sw), orc.swizzle_scales(rs), "swizzled")
+
+
+# ------------------------------------------------------------ strict FP8 rows
+def _all_pairs_input():
+    """Every (group max, block exponent) pair: rows of one 1x128 group whose
+    four blocks have exponents (e, mx, e, e); the 64 code bytes of row i are
+    64 * (i % 4) .. + 63, so every code byte meets every few pairs."""
+    rows_c, rows_s = [], []
+    i = 0
+    for mx in range(256):
+        for e in range(0, mx + 1):
+            rows_c.append((np.arange(64) + 64 * (i % 4)).astype(np.uint8))
+            rows_s.append(np.array([e, mx, e, e], np.uint8))
+            i += 1
+    return np.stack(rows_c), np.stack(rows_s)
+
+
+def test_fp8_rows_strict_all_exponent_pairs(cuda, orc):
+    c, s = _all_pairs_input()
+    q, so = H.to_fp8_rows(torch.from_numpy(c).to(cuda), torch.from_numpy(s).to(cuda),
+                          name="mxb_per_token_Mxfp4ToFp8_strict")
+    rq, rso = orc.mxfp4_to_fp8_rows_strict(c, s)
+    H.assert_bytes_equal(H.np_f32(so).view(np.uint32), rso.view(np.uint32), "scales")
+    H.assert_bytes_equal(H.np_u8(q), rq, "fp8")
+    # zero codes are true zeros; the default path wraps some of them to +-448
+    z = (c & 0x0F) == 0
+    lo = H.np_u8(q)[:, 0::2][z]
+    assert set(np.unique(lo).tolist()) <= {0x00}
+    dq, _ = H.to_fp8_rows(torch.from_numpy(c).to(cuda), torch.from_numpy(s).to(cuda))
+    assert (H.np_u8(dq)[:, 0::2][z] != 0).any()
+
+
+def test_fp8_rows_strict_config3_slice(cuda, orc):
+    c, s = syn.config3(2048, 8192, seed=2)
+    q, so = H.to_fp8_rows(c.to(cuda), s.to(cuda), name="mxb_per_token_Mxfp4ToFp8_strict")
+    rq, rso = orc.mxfp4_to_fp8_rows_strict(c.numpy(), s.numpy())
+    H.assert_bytes_equal(H.np_f32(so).view(np.uint32), rso.view(np.uint32), "scales")
+    H.assert_bytes_equal(H.np_u8(q), rq, "fp8")
+    # against the true values in float64: the E4M3 of the exact quotient
+    blk = np.repeat(s.numpy().astype(np.int64), 32, axis=1)           # per element exponent
+    nib = np.stack([c.numpy() & 0xF, c.numpy() >> 4], -1).reshape(c.shape[0], -1)
+    mag = np.array([0, .5, 1, 1.5, 2, 3, 4, 6])[nib & 7] * np.where(nib & 8, -1, 1)
+    g = np.repeat(rso.T.astype(np.float64), 128, axis=1)
+    true = mag * np.exp2(blk - 127.0) / g
+    got = H.np_u8(q).view(np.uint8)
+    gotf = torch.from_numpy(got).view(torch.float8_e4m3fn).float().numpy()
+    ref8 = torch.from_numpy(true.astype(np.float32)).to(torch.float8_e4m3fn).float().numpy()
+    np.testing.assert_array_equal(gotf, ref8)
+
+
+# ------------------------------------------------------------ per-row FP8
+@pytest.mark.parametrize("M,Kb", [(1, 16), (7, 8192), (64, 3584), (33, 16384), (512, 8192)])
+def test_fp8_rowscale(cuda, orc, M, Kb):
+    c, s = syn.config3(M, Kb, seed=M + Kb)
+    cn, sn = c.numpy().copy(), s.numpy().copy()
+    if M > 3:
+        sn[1, 0] = 255            # an infinite block scale (Inf and 0*Inf = NaN values)
+        sn[2, :] = 0              # a row of zero scales -> all zeros, amax = eps
+        cn[3, :] = 0x88           # a row of -0 codes
+    q, so = H.to_fp8_rowscale(torch.from_numpy(cn).to(cuda), torch.from_numpy(sn).to(cuda))
+    rq, rso = orc.mxfp4_to_fp8_rowscale(cn, sn)
+    H.assert_bytes_equal(H.np_f32(so).view(np.uint32), rso.view(np.uint32), "scales")
+    H.assert_bytes_equal(H.np_u8(q), rq, "fp8")
+
+
+def test_fp8_rowscale_matches_torch_fp32(cuda, orc):
+    """Against a plain torch float32 statement of the same op (dequantize, row
+    amax, scale, clamp, E4M3), on finite inputs."""
+    c, s = syn.config3(256, 4096, seed=11)
+    q, so = H.to_fp8_rowscale(c.to(cuda), s.to(cuda))
+    x = H.dequant_bf16(c.to(cuda), s.to(cuda)).float()
+    amax = x.abs().amax(1).clamp_min(1e-10)
+    c448 = torch.full_like(amax, 448.0)  # tensor / tensor: IEEE division (a scalar
+    # divisor would be applied as a multiply by its reciprocal)
+    ref = (x * (c448 / amax)[:, None]).clamp(-448, 448).to(torch.float8_e4m3fn)
+    assert torch.equal(so, amax / c448)
+    assert torch.equal(q.view(torch.uint8), ref.view(torch.uint8))

