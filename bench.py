@@ -143,8 +143,114 @@ def run_reference(args):
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    ref_gpu = time_reference_gpu_kernels(args)
+    if ref_gpu is not None:
+        line["ref_gpu_kernels"] = ref_gpu
     print(json.dumps(line), file=_OUT, flush=True)
     return 0
+
+
+def time_reference_gpu_kernels(args):
+    """The reference's own CUDA kernels (code/kernel/*.cu compiled unmodified for
+    sm_100a into oracle/_ref/omo_ref by oracle/build_ref.py) timed on this box's
+    GPU on every op's BASELINE shape, under the same op names as the B200 arm's
+    `ops`, so that each of this library's kernels has the reference kernel's
+    time beside it.  Q-col is timed as the reference path runs it: the
+    transpose copy (`.t().contiguous()`) followed by the rowwise quantize.
+    Returns None without a GPU or without the built reference."""
+    try:
+        import torch
+        if not torch.cuda.is_available():
+            return None
+        import importlib
+        d = ROOT / "oracle" / "_ref"
+        if not any(d.glob("omo_ref*.so")):
+            return {"unavailable": "oracle/_ref/omo_ref not built"}
+        sys.path.insert(0, str(d))
+        ref = importlib.import_module("omo_ref")
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+    from mxfp4_b200 import synthetic as syn
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    peak, _ = measured_peaks()
+    res = {}
+
+    def timeit(name, fn, alg_bytes, n=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = a.elapsed_time(b) / n
+        gbs = alg_bytes / (ms * 1e-3) / 1e9
+        res[name] = {"us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+
+    x = syn.config2().to(dev)
+    q = torch.empty(M2, K2 // 2, dtype=torch.uint8, device=dev)
+    s = torch.empty(M2, K2 // 32, dtype=torch.uint8, device=dev)
+    qc = torch.empty(K2, M2 // 2, dtype=torch.uint8, device=dev)
+    scc = torch.empty(K2, M2 // 32, dtype=torch.uint8, device=dev)
+    timeit("quant_rows_config2",
+           lambda: ref.omo_per_token_group_quant_fp4(x, q, s, 32, 1e-10, -6.0, 6.0, False),
+           M2 * K2 * 2 + M2 * K2 // 2 + M2 * K2 // 32)
+
+    def rowcol():
+        ref.omo_per_token_group_quant_fp4(x, q, s, 32, 1e-10, -6.0, 6.0, False)
+        ref.omo_per_token_group_quant_fp4(x.t().contiguous(), qc, scc, 32, 1e-10, -6.0, 6.0,
+                                          False)
+    timeit("quant_rowcol_config2", rowcol, ALG_BYTES_ROWCOL)
+    del x, q, s, qc, scc
+
+    c, sc = (t.to(dev) for t in syn.config3())
+    M3, Kb3 = c.shape
+    out = torch.empty(M3, 2 * Kb3, dtype=torch.bfloat16, device=dev)
+    dummy = torch.empty(M3, 2 * Kb3 // 128, dtype=torch.float32, device=dev)
+    timeit("dequant_bf16_config3",
+           lambda: ref.omo_per_token_Mxfp4ToBf16_dequant(c, sc, out, dummy, 32, 1e-10, -6.0, 6.0,
+                                                         False),
+           M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 4)
+    del out, dummy
+    f8 = torch.empty(M3, 2 * Kb3, dtype=torch.float8_e4m3fn, device=dev)
+    fs = torch.empty(Kb3 // 64, M3, dtype=torch.float32, device=dev)
+    timeit("mxfp4_to_fp8_rows_config3",
+           lambda: ref.omo_per_token_Mxfp4ToFp8(c, sc, f8, fs, 128, 1e-10, -6.0, 6.0, False),
+           M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + (Kb3 // 64) * M3 * 4)
+    del fs
+    f8t = f8.view(2 * Kb3, M3)
+    fcs = torch.empty(M3 // 128, 2 * Kb3, dtype=torch.float32, device=dev)
+    timeit("mxfp4_to_fp8_col_config3",
+           lambda: ref.omo_per_token_Mxfp4ToFp8_col(c, sc, f8t, fcs, 128, 1e-10, -6.0, 6.0, False),
+           M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fcs.numel() * 4)
+    timeit("mxfp4_to_fp8_colT_config3",
+           lambda: ref.omo_per_token_Mxfp4RowToBf16ToFp8Col(c, sc, f8t, fcs, 1e-10),
+           M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fcs.numel() * 4)
+    for name, mult in (("mxfp4_to_fp8_colT_msplit8_config3", 1),
+                       ("mxfp4_to_fp8_colT_msplit8x128_config3", 128)):
+        m_splits = syn.config3_splits(M3, 8, mult)
+        so, sco, acc, accs = [], [], 0, 0
+        for m in m_splits:
+            so.append(acc)
+            sco.append(accs)
+            acc += m
+            accs += (m + 127) // 128
+        i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
+        dm, dso, dsco = i32(m_splits), i32(so), i32(sco)
+        f8f = f8.view(-1)
+        fss = torch.empty(accs, 2 * Kb3, dtype=torch.float32, device=dev)
+        timeit(name,
+               lambda: ref.omo_per_token_Mxfp4RowToBf16ToFp8Col_msplit(
+                   c, sc, f8f, fss, dm, dso, dsco, max(m_splits), 1e-10),
+               M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + fss.numel() * 4)
+    return {"what": "reference code/kernel/*.cu built unmodified for sm_100a (oracle/_ref), "
+                    "CUDA events, device-resident inputs, same shapes and byte counts as the "
+                    "B200 arm's ops", "ops": res}
 
 
 def cpu_baseline_sample():
@@ -285,6 +391,7 @@ def main():
     del xh, outs_h, ws
 
     ops = {} if args.no_ops else time_other_ops(dev, stream, peak)
+    sharded4 = time_sharded_config4(dev, stream, world, rank, args.steps)
     ep = time_ep(dev, stream, world, rank, args) if world > 1 else None
     if rank != 0:
         if world > 1:
@@ -311,6 +418,7 @@ def main():
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
         "ops": ops,
+        "sharded_config4": sharded4,
         "ep": ep,
     }
     print(json.dumps(line), file=_OUT, flush=True)
@@ -319,7 +427,7 @@ def main():
     return 0
 
 
-NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool (900 nominal)
+NVLINK_GBS = 900.0  # NVLink 5 per direction per GPU (nominal; the roofline denominator)
 
 
 def time_ep(dev, stream, world, rank, args):
@@ -371,30 +479,127 @@ def time_ep(dev, stream, world, rank, args):
     from mxfp4_b200 import capi
     from mxfp4_b200.ep import P2PDispatcher
     p2p = P2PDispatcher(None, tcap=T, hidden=H, topk=8, num_experts=256)
-    for _ in range(3):
-        p2p.step(x, idx, w)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([e0.elapsed_time(e1) / n], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms2 = timed(lambda: p2p.step(x, idx, w))
+    ms_disp = timed(lambda: p2p.dispatch_only(x, idx, w))
+    # device time of each phase (events between the enqueued phases, the stream
+    # kept full so that host gaps do not show), mean over n steps, max over ranks
+    names = ["route", "counts", "dispatch", "barrier1", "return", "barrier2", "combine"]
+    evs = []
+
+    def mark(_name):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        evs[-1].append(ev)
+
     torch.cuda.synchronize(dev)
     dist.barrier()
-    e0.record(stream)
     for _ in range(n):
-        p2p.step(x, idx, w)
-    e1.record(stream)
+        start = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        evs.append([start])
+        p2p.step(x, idx, w, mark=mark)
     torch.cuda.synchronize(dev)
-    ms2 = e0.elapsed_time(e1) / n
-    t = torch.tensor([ms2], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms2 = float(t.item())
+    ph = torch.tensor([sum(s[i].elapsed_time(s[i + 1]) for s in evs) / n for i in range(len(names))],
+                      dtype=torch.float64, device=dev)
+    dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+    phases_us = {nm: round(float(v) * 1e3, 1) for nm, v in zip(names, ph.tolist())}
     timeouts = int(capi.load().mxb_ep_wait_timeouts())
     dist.barrier()
     p2p.close()
+    # dispatch alone: the MXFP4 rows (+ routing metadata) that cross NVLink
+    d_bytes = torch.tensor([float(max(send_remote, recv_remote) * rb)], dtype=torch.float64,
+                           device=dev)
+    dist.all_reduce(d_bytes, op=dist.ReduceOp.MAX)
+    d_floor_ms = float(d_bytes.item()) / (NVLINK_GBS * 1e9) * 1e3
     return {"metric": "ep_dispatch_combine_tokens_per_s", "value": round(world * T / (ms2 * 1e-3), 1),
             "unit": "tokens/s", "ms_per_step": round(ms2, 4), "tokens_per_rank": T, "hidden": H,
             "experts": 256, "topk": 8, "payload": "mxfp4 dispatch, bf16 combine",
             "transport": "fused quantize + NVLink peer stores (CUDA IPC), device barriers",
             "wait_timeouts": timeouts, "nccl_baseline": nccl,
+            "phases_us": phases_us,
             "nvlink_roofline": {"bound": "nvlink", "bytes_per_gpu_direction": int(bt.item()),
-                                "peak_gbs": NVLINK_GBS, "floor_ms": round(floor_ms, 4),
-                                "frac": round(floor_ms / ms2, 4)}}
+                                "peak_gbs": NVLINK_GBS, "peak_source": "nominal NVLink 5",
+                                "floor_ms": round(floor_ms, 4),
+                                "frac": round(floor_ms / ms2, 4)},
+            "dispatch": {"metric": "ep_dispatch_tokens_per_s",
+                         "value": round(world * T / (ms_disp * 1e-3), 1),
+                         "ms_per_step": round(ms_disp, 4),
+                         "what": "route + count exchange + fused quantize/peer stores + barrier",
+                         "nvlink_roofline": {"bytes_per_gpu_direction": int(d_bytes.item()),
+                                             "peak_gbs": NVLINK_GBS,
+                                             "floor_ms": round(d_floor_ms, 4),
+                                             "frac": round(d_floor_ms / ms_disp, 4)}}}
+
+
+def time_sharded_config4(dev, stream, world, rank, steps):
+    """BASELINE config 4 ("rows sharded across 1/2/4/8 GPUs"): the [32768, 7168]
+    BF16 tensor split into `world` contiguous row ranges, each rank running the
+    per-token FP8 quantize and then the dequantize of its own rows (no
+    collective in the data path).  Total work is fixed (strong scaling); GB/s =
+    the whole tensor's algorithmic bytes / max-over-ranks time."""
+    import torch
+    import torch.distributed as dist
+
+    from mxfp4_b200 import capi
+    from mxfp4_b200 import synthetic as syn
+
+    x = syn.config4()
+    M, K = x.shape
+    r0, r1 = rank * M // world, (rank + 1) * M // world
+    xs = x[r0:r1].contiguous().to(dev)
+    del x
+    m = r1 - r0
+    q = torch.empty(m, K, dtype=torch.uint8, device=dev)
+    s = torch.empty(m, dtype=torch.float32, device=dev)
+    out = torch.empty_like(xs)
+    sh = stream.cuda_stream
+    alg = M * K * 2 + M * K + M * 4
+
+    def quant():
+        capi.call("mxb_per_token_quant_fp8", xs.data_ptr(), m, K, q.data_ptr(), s.data_ptr(),
+                  1e-10, sh)
+
+    def dequant():
+        capi.call("mxb_per_token_dequant_fp8", q.data_ptr(), s.data_ptr(), m, K, out.data_ptr(), sh)
+
+    res = {}
+    n = max(10, min(steps, 50))
+    for name, fn in (("quant", quant), ("dequant", dequant)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = a.elapsed_time(b) / n
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        res[name] = {"us": round(ms * 1e3, 2), "gbs": round(alg / (ms * 1e-3) / 1e9, 1)}
+    return {"workload": "config4 per-token FP8 quantize / dequantize, BF16 [32768, 7168] "
+                        f"row-sharded over {world} GPU(s)", "scaling": "strong",
+            "rows_per_gpu": m, **res}
 
 
 def time_other_ops(dev, stream, peak, only=None):
@@ -434,11 +639,13 @@ def time_other_ops(dev, stream, peak, only=None):
             return
         res[name] = {"us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
 
-    C3 = ("dequant_bf16_config3", "mxfp4_to_fp8_rows_config3", "mxfp4_to_fp8_col_config3",
+    C3 = ("dequant_bf16_config3", "mxfp4_to_fp8_rows_config3", "mxfp4_to_fp8_rows_strict_config3",
+          "mxfp4_to_fp8_rowscale_config3", "mxfp4_to_fp8_col_config3",
           "mxfp4_to_fp8_colT_config3", "mxfp4_to_fp8_colT_msplit8_config3",
           "mxfp4_to_fp8_colT_msplit8x128_config3")
     # Q-row alone on config 2
-    if want("quant_rows_config2", "quant_fused_fp8_config2", "swiglu_quant_config2"):
+    if want("quant_rows_config2", "quant_fused_fp8_config2", "swiglu_quant_config2",
+            "quant_rowcol_ocp_config2"):
         _ops_config2(dev, sh, timeit, capi, syn)
     if want(*C3):
         _ops_config3(dev, sh, timeit, capi, syn)
@@ -460,6 +667,14 @@ def _ops_config2(dev, sh, timeit, capi, syn):
         lambda: capi.call("mxb_per_token_group_quant_fp4", x.data_ptr(), M2, K2, K2, q.data_ptr(),
                           s.data_ptr(), 32, 1e-10, -6.0, 6.0, 0, sh),
         M2 * K2 * 2 + M2 * K2 // 2 + M2 * K2 // 32)
+    # the headline's rowwise + columnwise quantize under the OCP scale rule
+    qc = torch.empty(K2, M2 // 2, dtype=torch.uint8, device=dev)
+    sc2 = torch.empty(K2, M2 // 32, dtype=torch.uint8, device=dev)
+    timeit("quant_rowcol_ocp_config2",
+        lambda: capi.call("mxb_quantize_mxfp4", x.data_ptr(), M2, K2, K2, q.data_ptr(),
+                          s.data_ptr(), qc.data_ptr(), sc2.data_ptr(), None, 1, sh),
+        ALG_BYTES_ROWCOL)
+    del qc, sc2
     # Q-row fused with its rowwise FP8 conversion (omo_per_token_group_quant_fp4_fused_ToFp8)
     f8q = torch.empty(M2, K2, dtype=torch.uint8, device=dev)
     f8s = torch.empty(K2 // 128, M2, dtype=torch.float32, device=dev)
@@ -493,7 +708,17 @@ def _ops_config3(dev, sh, timeit, capi, syn):
         lambda: capi.call("mxb_per_token_Mxfp4ToFp8", c.data_ptr(), sc.data_ptr(), M3, Kb3,
                           f8.data_ptr(), fs.data_ptr(), sh),
         M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + (Kb3 // 64) * M3 * 4)
+    timeit("mxfp4_to_fp8_rows_strict_config3",
+        lambda: capi.call("mxb_per_token_Mxfp4ToFp8_strict", c.data_ptr(), sc.data_ptr(), M3, Kb3,
+                          f8.data_ptr(), fs.data_ptr(), sh),
+        M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + (Kb3 // 64) * M3 * 4)
     del fs
+    frs = torch.empty(M3, dtype=torch.float32, device=dev)
+    timeit("mxfp4_to_fp8_rowscale_config3",
+        lambda: capi.call("mxb_per_token_Mxfp4ToFp8_rowscale", c.data_ptr(), sc.data_ptr(), M3,
+                          Kb3, f8.data_ptr(), frs.data_ptr(), 1e-10, sh),
+        M3 * Kb3 + M3 * Kb3 // 16 + M3 * Kb3 * 2 + M3 * 4)
+    del frs
     fcs = torch.empty(M3 // 128, 2 * Kb3, dtype=torch.float32, device=dev)
     timeit("mxfp4_to_fp8_col_config3",
         lambda: capi.call("mxb_per_token_Mxfp4ToFp8_col", c.data_ptr(), sc.data_ptr(), M3, Kb3,

@@ -248,11 +248,8 @@ class P2PDispatcher:
         import ctypes
         return self.bases.data_ptr(), ctypes.byref(self.layout)
 
-    def step(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor,
-             expert_fn=None) -> torch.Tensor:
-        """Dispatch -> experts -> combine.  Without expert_fn every expert is the
-        identity and a row returns as its dequantized token times its local
-        routing-weight sum (fused into the return kernel)."""
+    def _dispatch_phase(self, x, topk_idx, topk_w, mark):
+        """Routing, count exchange, fused quantize + peer stores, barrier."""
         T = x.shape[0]
         s = torch.cuda.current_stream(x.device).cuda_stream
         topk_idx = topk_idx.to(torch.int64).contiguous()
@@ -261,19 +258,60 @@ class P2PDispatcher:
         capi.call("mxb_ep_route", topk_idx.data_ptr(), T, topk_idx.shape[1],
                   self.num_experts // self.world, self.world, within.data_ptr(),
                   send_counts.data_ptr(), s)
+        mark("route")
         parity = self.step_no & 1
         e = 3 * self.step_no
         bases, lp = self._args()
         capi.call("mxb_ep_p2p_counts", bases, lp, send_counts.data_ptr(), parity, e + 1, s)
+        mark("counts")
         capi.call("mxb_ep_p2p_dispatch", x.data_ptr(), T, within.data_ptr(),
                   topk_idx.data_ptr(),
                   topk_w.float().contiguous().data_ptr(), bases, lp, parity, s)
+        mark("dispatch")
         capi.call("mxb_ep_p2p_barrier", bases, lp, e + 2, s)
+        mark("barrier1")
+        return within, send_counts, parity, e
+
+    def dispatch_only(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor,
+                      mark=None) -> None:
+        """The dispatch half of a step: after it every rank's receive rows
+        (self.wire, grouped by source rank) hold the MXFP4 wire rows routed to
+        it.  Used to time the dispatch alone; a full step() may follow."""
+        self._dispatch_phase(x, topk_idx, topk_w, mark or (lambda _n: None))
+        self.step_no += 1
+
+    def step(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor,
+             expert_fn=None, mark=None) -> torch.Tensor:
+        """Dispatch -> experts -> combine.  Without expert_fn every expert is the
+        identity and a row returns as its dequantized token times its local
+        routing-weight sum (fused into the return kernel).  mark(name), if
+        given, is called after each phase is enqueued (route, counts, dispatch,
+        barrier1, return, barrier2, combine), e.g. to record CUDA events."""
+        mark = mark or (lambda _n: None)
+        T = x.shape[0]
+        s = torch.cuda.current_stream(x.device).cuda_stream
+        within, send_counts, parity, e = self._dispatch_phase(x, topk_idx, topk_w, mark)
+        bases, lp = self._args()
         y = None if expert_fn is None else expert_fn(self.wire).contiguous()
         capi.call("mxb_ep_p2p_return", None if y is None else y.data_ptr(), bases, lp, parity, s)
+        mark("return")
         capi.call("mxb_ep_p2p_barrier", bases, lp, e + 3, s)
+        mark("barrier2")
         out = torch.empty(T, self.hidden, dtype=torch.bfloat16, device=x.device)
         capi.call("mxb_ep_p2p_combine", self.back.data_ptr(), T, self.hidden, within.data_ptr(),
                   send_counts.data_ptr(), self.world, out.data_ptr(), s)
+        mark("combine")
         self.step_no += 1
         return out
+
+    def check(self) -> None:
+        """Raises PeerTimeout if a cross-GPU wait of this process gave up since
+        the last check (a peer is late or gone, and the outputs of the steps
+        since then are invalid).  Synchronises the device."""
+        n = int(capi.load().mxb_ep_reset_wait_timeouts())
+        if n:
+            raise PeerTimeout(f"rank {self.rank}: {n} cross-GPU wait(s) gave up")
+
+
+class PeerTimeout(RuntimeError):
+    """A bounded cross-GPU wait of the fused dispatcher ran out."""
