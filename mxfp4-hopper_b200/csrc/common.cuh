@@ -163,6 +163,68 @@ __device__ __forceinline__ void e2m1x4_to_bf16x4(uint32_t w, uint32_t& out0, uin
   out1 = prmt(lo, hi, 0x7362u);
 }
 
+// Eight E2M1 codes (one code word: value i in nibble i) times the factor sf
+// -> eight floats; with sf an E8M0 power of two these are exactly the
+// reference's BF16 products widened:
+// Blackwell's cvt.rn.f16x2.e2m1x2 decodes a code byte, the sm_100
+// mixed-precision add.rn.f32.f16 widens each half (adding -0 keeps the sign of
+// zero), and mul.rn.f32x2 scales by the power of two sf (exact; sf = 0 gives
+// zeros, sf = Inf gives Inf or the NaN of 0 * Inf, as the BF16 product does).
+__device__ __forceinline__ void decode8_scaled(uint32_t w, float sf, float (&o)[8]) {
+  asm("{\n"
+      ".reg .b8 b0, b1, b2, b3;\n"
+      ".reg .b32 h0, h1, h2, h3;\n"
+      ".reg .b16 p0, p1, p2, p3, p4, p5, p6, p7;\n"
+      ".reg .f32 f0, f1, f2, f3, f4, f5, f6, f7;\n"
+      ".reg .b64 x0, x1, x2, x3, s2;\n"
+      "mov.b32 {b0, b1, b2, b3}, %8;\n"
+      "cvt.rn.f16x2.e2m1x2 h0, b0;\n"
+      "cvt.rn.f16x2.e2m1x2 h1, b1;\n"
+      "cvt.rn.f16x2.e2m1x2 h2, b2;\n"
+      "cvt.rn.f16x2.e2m1x2 h3, b3;\n"
+      "mov.b32 {p0, p1}, h0;\n"
+      "mov.b32 {p2, p3}, h1;\n"
+      "mov.b32 {p4, p5}, h2;\n"
+      "mov.b32 {p6, p7}, h3;\n"
+      "add.rn.f32.f16 f0, p0, 0f80000000;\n"
+      "add.rn.f32.f16 f1, p1, 0f80000000;\n"
+      "add.rn.f32.f16 f2, p2, 0f80000000;\n"
+      "add.rn.f32.f16 f3, p3, 0f80000000;\n"
+      "add.rn.f32.f16 f4, p4, 0f80000000;\n"
+      "add.rn.f32.f16 f5, p5, 0f80000000;\n"
+      "add.rn.f32.f16 f6, p6, 0f80000000;\n"
+      "add.rn.f32.f16 f7, p7, 0f80000000;\n"
+      "mov.b64 s2, {%9, %9};\n"
+      "mov.b64 x0, {f0, f1};\n"
+      "mov.b64 x1, {f2, f3};\n"
+      "mov.b64 x2, {f4, f5};\n"
+      "mov.b64 x3, {f6, f7};\n"
+      "mul.rn.f32x2 x0, x0, s2;\n"
+      "mul.rn.f32x2 x1, x1, s2;\n"
+      "mul.rn.f32x2 x2, x2, s2;\n"
+      "mul.rn.f32x2 x3, x3, s2;\n"
+      "mov.b64 {%0, %1}, x0;\n"
+      "mov.b64 {%2, %3}, x1;\n"
+      "mov.b64 {%4, %5}, x2;\n"
+      "mov.b64 {%6, %7}, x3;\n"
+      "}"
+      : "=f"(o[0]), "=f"(o[1]), "=f"(o[2]), "=f"(o[3]), "=f"(o[4]), "=f"(o[5]), "=f"(o[6]),
+        "=f"(o[7])
+      : "r"(w), "f"(sf));
+}
+
+// Two floats per cvt: four E4M3 bytes of (a0, a1, b0, b1), RNE, saturating.
+__device__ __forceinline__ uint32_t cvt_e4m3x4(float a0, float a1, float b0, float b1) {
+  uint32_t r;
+  asm("{\n .reg .b16 lo, hi;\n"
+      " cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n"
+      " cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n"
+      " mov.b32 %0, {lo, hi};\n}"
+      : "=r"(r)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+  return r;
+}
+
 // E8M0 byte -> float via the reference's BF16 reinterpretation.
 __device__ __forceinline__ float e8m0_to_f(uint32_t e) { return __uint_as_float(e << 23); }
 

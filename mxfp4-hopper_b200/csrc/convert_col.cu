@@ -97,8 +97,10 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
   uint64_t* bar = reinterpret_cast<uint64_t*>(red + 8);
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int rb = warp >> 1, hh = warp & 1;  // 32-row block, 64-byte half of the tile
-  const int64_t row0 = (int64_t)blockIdx.y * 128;
-  const int64_t cb0 = (int64_t)blockIdx.x * 128;  // first code byte of the tile
+  // row blocks fastest: CTAs running together extend the same 256 output rows
+  // (adjacent 128-byte runs), so the transposed writes merge into long runs
+  const int64_t row0 = (int64_t)blockIdx.x * 128;
+  const int64_t cb0 = (int64_t)blockIdx.y * 128;  // first code byte of the tile
   const int64_t S = Kb / 16;
   const int r = rb * 32 + lane;
 
@@ -377,67 +379,6 @@ __device__ __forceinline__ bool colT_factors(uint32_t sc, int r, uint32_t* fac) 
     special = special || e == 255u;
   }
   return special;
-}
-
-// Eight E2M1 codes (one code word: value i in nibble i) times the E8M0
-// factor sf -> eight floats, exactly the reference's BF16 products widened:
-// Blackwell's cvt.rn.f16x2.e2m1x2 decodes a code byte, the sm_100
-// mixed-precision add.rn.f32.f16 widens each half (adding -0 keeps the sign of
-// zero), and mul.rn.f32x2 scales by the power of two sf (exact; sf = 0 gives
-// zeros, sf = Inf gives Inf or the NaN of 0 * Inf, as the BF16 product does).
-__device__ __forceinline__ void decode8_scaled(uint32_t w, float sf, float (&o)[8]) {
-  asm("{\n"
-      ".reg .b8 b0, b1, b2, b3;\n"
-      ".reg .b32 h0, h1, h2, h3;\n"
-      ".reg .b16 p0, p1, p2, p3, p4, p5, p6, p7;\n"
-      ".reg .f32 f0, f1, f2, f3, f4, f5, f6, f7;\n"
-      ".reg .b64 x0, x1, x2, x3, s2;\n"
-      "mov.b32 {b0, b1, b2, b3}, %8;\n"
-      "cvt.rn.f16x2.e2m1x2 h0, b0;\n"
-      "cvt.rn.f16x2.e2m1x2 h1, b1;\n"
-      "cvt.rn.f16x2.e2m1x2 h2, b2;\n"
-      "cvt.rn.f16x2.e2m1x2 h3, b3;\n"
-      "mov.b32 {p0, p1}, h0;\n"
-      "mov.b32 {p2, p3}, h1;\n"
-      "mov.b32 {p4, p5}, h2;\n"
-      "mov.b32 {p6, p7}, h3;\n"
-      "add.rn.f32.f16 f0, p0, 0f80000000;\n"
-      "add.rn.f32.f16 f1, p1, 0f80000000;\n"
-      "add.rn.f32.f16 f2, p2, 0f80000000;\n"
-      "add.rn.f32.f16 f3, p3, 0f80000000;\n"
-      "add.rn.f32.f16 f4, p4, 0f80000000;\n"
-      "add.rn.f32.f16 f5, p5, 0f80000000;\n"
-      "add.rn.f32.f16 f6, p6, 0f80000000;\n"
-      "add.rn.f32.f16 f7, p7, 0f80000000;\n"
-      "mov.b64 s2, {%9, %9};\n"
-      "mov.b64 x0, {f0, f1};\n"
-      "mov.b64 x1, {f2, f3};\n"
-      "mov.b64 x2, {f4, f5};\n"
-      "mov.b64 x3, {f6, f7};\n"
-      "mul.rn.f32x2 x0, x0, s2;\n"
-      "mul.rn.f32x2 x1, x1, s2;\n"
-      "mul.rn.f32x2 x2, x2, s2;\n"
-      "mul.rn.f32x2 x3, x3, s2;\n"
-      "mov.b64 {%0, %1}, x0;\n"
-      "mov.b64 {%2, %3}, x1;\n"
-      "mov.b64 {%4, %5}, x2;\n"
-      "mov.b64 {%6, %7}, x3;\n"
-      "}"
-      : "=f"(o[0]), "=f"(o[1]), "=f"(o[2]), "=f"(o[3]), "=f"(o[4]), "=f"(o[5]), "=f"(o[6]),
-        "=f"(o[7])
-      : "r"(w), "f"(sf));
-}
-
-// Two floats per cvt: four E4M3 bytes of (a0, a1, b0, b1), RNE, saturating.
-__device__ __forceinline__ uint32_t cvt_e4m3x4(float a0, float a1, float b0, float b1) {
-  uint32_t r;
-  asm("{\n .reg .b16 lo, hi;\n"
-      " cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n"
-      " cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n"
-      " mov.b32 %0, {lo, hi};\n}"
-      : "=r"(r)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-  return r;
 }
 
 // max(|a|, |b|, |c|), NaN inputs ignored (sm_100 three-input max).
@@ -736,9 +677,6 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
       col_qs[t] = qs;
       // NaN products are possible only with an Inf amax or an E8M0 byte of 255
       col_clamp[t] = (mb >= 0x7F800000u || tile_special) ? 1 : 0;
-      // tile i+1's factors into the other buffer (last read in tile i-1's step
-      // 1); the barrier below orders these stores before tile i+1's step 1
-      if (has_next) special_next = colT_factors(sc_next, t, fac + ((i + 1) & 1) * 512);
     }
     __syncthreads();
 
@@ -771,6 +709,10 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
             make_uint2(cvt_e4m3x4(q[0], q[1], q[2], q[3]), cvt_e4m3x4(q[4], q[5], q[6], q[7]));
       }
     }
+    // tile i+1's factors into the other buffer (last read in tile i-1's step
+    // 1); the barrier below orders these stores before tile i+1's step 1, and
+    // steps 1-3 of this tile have covered the scale load's latency
+    if (t < 128 && has_next) special_next = colT_factors(sc_next, t, fac + ((i + 1) & 1) * 512);
     __syncthreads();
 
     // ---- 4. output rows n (128 FP8 bytes each), eight lanes per row: thread t
@@ -929,7 +871,7 @@ extern "C" mxb_status mxb_per_token_Mxfp4ToFp8_col(const void* input, const void
       cudaFuncSetAttribute((const void*)fp8_col_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kColSmem) == cudaSuccess;
   MXB_REQUIRE(attr_ok, MXB_ERR_CUDA, "mxfp4_to_fp8_col: cannot reserve shared memory");
-  const dim3 grid((unsigned)(Kb / 128), (unsigned)(M / 128));
+  const dim3 grid((unsigned)(M / 128), (unsigned)(Kb / 128));
   fp8_col_kernel<<<grid, kThreads, kColSmem, to_cuda(stream)>>>(tmap, (const uint8_t*)input_s, M,
                                                                 Kb, (uint8_t*)output_q,
                                                                 (float*)output_s);

@@ -15,6 +15,8 @@
 // which re-bases every block onto the group exponent in integer arithmetic;
 // zero codes in blocks more than six binades below the group maximum wrap to
 // +-448 exactly as on the reference.
+#include <cuda_bf16.h>
+
 #include "capi_util.h"
 #include "common.cuh"
 #include "fp8_lut.cuh"
@@ -69,21 +71,18 @@ __global__ void __launch_bounds__(256) dq_bf16_kernel(const uint8_t* __restrict_
 }
 
 // -------------------------------------------------------------- DQ-fp8-row
-// A lane converts 8 code bytes (16 elements, half a 32-element block) into one
-// 16-byte FP8 store; eight lanes cover one 1x128 group and read the group's
-// four E8M0 bytes as one word.  The element arithmetic is a lookup in the
-// compile-time table row for d = max_e - e (fp8_lut.cuh).  Four chunks per lane
-// are in flight per iteration.
+// A lane converts one 32-element block: 16 code bytes (one 16-byte load) and
+// its E8M0 byte into 32 FP8 bytes (two 16-byte stores).  Blocks are contiguous
+// in the flat code array and so are their scale bytes, so lane b reads scale
+// byte b; the four lanes of a 1x128 group are adjacent (the groups of a row
+// start at multiples of 4 blocks), so the group max is two shuffles.  The
+// element arithmetic is a lookup in the compile-time table row for
+// d = max_e - e (fp8_lut.cuh), four nibbles per lookup.  kRowBlk blocks per
+// lane are in flight per iteration.
 __device__ const Fp8Lut g_lut_row = make_fp8_lut(false);
 __device__ const Fp8Lut g_lut_row_strict = make_fp8_lut_strict();
 
-__device__ __forceinline__ uint32_t max_u8x4(uint32_t s) {
-  uint32_t a = max(s & 0xFFu, (s >> 8) & 0xFFu);
-  uint32_t b = max((s >> 16) & 0xFFu, s >> 24);
-  return max(a, b);
-}
-
-constexpr int kFp8RowUnroll = 4;
+constexpr int kRowBlk = 4;  // measured on config 3: 1 -> 80.1 us, 2 -> 83.6 us, 4 -> 79.6 us
 
 template <bool kStrict>
 __global__ void __launch_bounds__(256) dq_fp8_row_kernel(const uint8_t* __restrict__ codes,
@@ -91,55 +90,53 @@ __global__ void __launch_bounds__(256) dq_fp8_row_kernel(const uint8_t* __restri
                                                          int64_t M, int64_t Kb,
                                                          uint8_t* __restrict__ out,
                                                          float* __restrict__ scales_out) {
-  const int64_t lanes_total = M * Kb / 8;  // one lane per 8 code bytes
+  const int64_t nblk = M * Kb / 16;
   const int64_t groups_per_row = Kb / 64;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x * kFp8RowUnroll;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * kRowBlk;
   const int lane = threadIdx.x & 31;
-  for (int64_t base = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) * kFp8RowUnroll;
-       base < lanes_total; base += stride) {
-    // all loads of the iteration first (codes, then the groups' scale words,
-    // then the table rows they select), then the arithmetic and the stores
-    uint2 w[kFp8RowUnroll];
-    uint32_t sw[kFp8RowUnroll];
+  const Fp8Lut& lut = kStrict ? g_lut_row_strict : g_lut_row;
+  for (int64_t base = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) * kRowBlk;
+       base < nblk; base += stride) {
+    uint4 c[kRowBlk];
+    uint32_t e[kRowBlk];
 #pragma unroll
-    for (int k = 0; k < kFp8RowUnroll; ++k) {
-      const int64_t l = base + k * 32 + lane;
-      if (l < lanes_total) {
-        w[k] = ld_stream_v2(codes + l * 8);
-        sw[k] = ld_stream_u32(scales + (l >> 3) * 4);
+    for (int k = 0; k < kRowBlk; ++k) {
+      const int64_t b = base + k * 32 + lane;
+      if (b < nblk) {
+        c[k] = ld_stream_v4(codes + b * 16);
+        e[k] = ld_stream_u8(scales + b);
       } else {
-        w[k] = make_uint2(0u, 0u);
-        sw[k] = 0u;
+        c[k] = make_uint4(0u, 0u, 0u, 0u);
+        e[k] = 0u;
       }
     }
-    uint32_t mx[kFp8RowUnroll];
-    uint4 t[kFp8RowUnroll];
 #pragma unroll
-    for (int k = 0; k < kFp8RowUnroll; ++k) {
-      const int64_t l = base + k * 32 + lane;
-      mx[k] = max_u8x4(sw[k]);
-      const uint32_t e = (sw[k] >> (8 * ((l >> 1) & 3))) & 0xFFu;
-      t[k] = __ldg(reinterpret_cast<const uint4*>((kStrict ? g_lut_row_strict : g_lut_row).v[mx[k] - e]));
-    }
-#pragma unroll
-    for (int k = 0; k < kFp8RowUnroll; ++k) {
-      const int64_t l = base + k * 32 + lane;
-      if (l >= lanes_total) continue;
-      const uint4 o = make_uint4(lut_lookup4(w[k].x, t[k].x, t[k].y, t[k].z, t[k].w),
-                                 lut_lookup4(w[k].x >> 16, t[k].x, t[k].y, t[k].z, t[k].w),
-                                 lut_lookup4(w[k].y, t[k].x, t[k].y, t[k].z, t[k].w),
-                                 lut_lookup4(w[k].y >> 16, t[k].x, t[k].y, t[k].z, t[k].w));
-      st_stream_v4(out + l * 16, o);
-      if ((l & 7) == 0) {
-        const int64_t grp = l >> 3;
+    for (int k = 0; k < kRowBlk; ++k) {
+      const int64_t b = base + k * 32 + lane;
+      uint32_t mx = max(e[k], __shfl_xor_sync(0xffffffffu, e[k], 1));
+      mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const uint4 t = __ldg(reinterpret_cast<const uint4*>(lut.v[mx - e[k]]));
+      if (b >= nblk) continue;
+      const uint4 o0 = make_uint4(lut_lookup4(c[k].x, t.x, t.y, t.z, t.w),
+                                  lut_lookup4(c[k].x >> 16, t.x, t.y, t.z, t.w),
+                                  lut_lookup4(c[k].y, t.x, t.y, t.z, t.w),
+                                  lut_lookup4(c[k].y >> 16, t.x, t.y, t.z, t.w));
+      const uint4 o1 = make_uint4(lut_lookup4(c[k].z, t.x, t.y, t.z, t.w),
+                                  lut_lookup4(c[k].z >> 16, t.x, t.y, t.z, t.w),
+                                  lut_lookup4(c[k].w, t.x, t.y, t.z, t.w),
+                                  lut_lookup4(c[k].w >> 16, t.x, t.y, t.z, t.w));
+      st_stream_v4(out + b * 32, o0);
+      st_stream_v4(out + b * 32 + 16, o1);
+      if ((lane & 3) == 0) {
+        const int64_t grp = b >> 2;
         int64_t r;
-        if (grp <= (int64_t)UINT32_MAX) {  // 32-bit division whenever it suffices
-          r = (uint32_t)grp / (uint32_t)groups_per_row;
+        if (grp <= (int64_t)UINT32_MAX && groups_per_row <= (int64_t)UINT32_MAX) {
+          r = (uint32_t)grp / (uint32_t)groups_per_row;  // 32-bit division whenever it suffices
         } else {
           r = grp / groups_per_row;
         }
         const int64_t gc = grp - r * groups_per_row;
-        scales_out[gc * M + r] = __uint_as_float(((mx[k] - 6u) & 0xFFu) << 23);
+        scales_out[gc * M + r] = __uint_as_float(((mx - 6u) & 0xFFu) << 23);
       }
     }
   }
@@ -151,101 +148,140 @@ __global__ void __launch_bounds__(256) dq_fp8_row_kernel(const uint8_t* __restri
 // per row, the per-token FP8 convention of this library (fp8_token.cu):
 //   amax = max(eps, max |x|) (NaN ignored), scale = amax / 448,
 //   q = E4M3(clamp(x * (448 / amax), +-448)).
-// One CTA per row; with kWords > 0 a thread keeps its kWords decoded 4-byte
-// code words (8 BF16 each) in registers between the amax and the quantize
-// pass, otherwise (long rows) it decodes the codes again from L1/L2.
+// One CTA per row.  A thread holds kChunks 16-byte code chunks (one 32-element
+// block each) in registers.  The row amax needs no decode: the largest value
+// of a block is its largest E2M1 magnitude times the block's factor, one
+// product per block, rounded to BF16 as the dequantize rounds it (NaN from
+// 0 * Inf never wins a float max).  The second pass decodes each chunk and
+// writes its 32 FP8 bytes.  kChunks = 0: rows too long for registers, codes
+// re-read (from L1/L2).
 constexpr int kRsThreads = 128;
 
-template <int kWords>
+__device__ __forceinline__ uint32_t vmax_u8x4(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("vmax4.u32.u32.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(0u));
+  return r;
+}
+
+// Largest |value| of one 32-element block as the dequantize produces it.
+__device__ __forceinline__ float block_amax(uint4 c, uint32_t e) {
+  uint32_t m = vmax_u8x4(vmax_u8x4(c.x & 0x07070707u, (c.x >> 4) & 0x07070707u),
+                         vmax_u8x4(c.y & 0x07070707u, (c.y >> 4) & 0x07070707u));
+  m = vmax_u8x4(m, vmax_u8x4(vmax_u8x4(c.z & 0x07070707u, (c.z >> 4) & 0x07070707u),
+                             vmax_u8x4(c.w & 0x07070707u, (c.w >> 4) & 0x07070707u)));
+  m = max(max(m & 0xFFu, (m >> 8) & 0xFFu), max((m >> 16) & 0xFFu, m >> 24));
+  // E2M1 magnitude of m, exactly: {0, .5, 1, 1.5, 2, 3, 4, 6}
+  const float mag = m < 2u ? 0.5f * (float)m : (float)((2u | (m & 1u)) << ((m >> 1) - 1u)) * 0.5f;
+  const float p = mag * e8m0_to_f(e);  // exact, or the float product the dequantize rounds
+  return __bfloat162float(__float2bfloat16_rn(p));
+}
+
+__device__ __forceinline__ void quant_chunk32(uint4 c, uint32_t e, float qs, uint8_t* dst) {
+  const uint32_t cw[4] = {c.x, c.y, c.z, c.w};
+  uint32_t o[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 d = dq_bf16_chunk(cw[j], e);
+    const uint32_t w[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float a0 = fminf(fmaxf(bf16lo_to_f(w[2 * h]) * qs, -448.0f), 448.0f);
+      const float a1 = fminf(fmaxf(bf16hi_to_f(w[2 * h]) * qs, -448.0f), 448.0f);
+      const float a2 = fminf(fmaxf(bf16lo_to_f(w[2 * h + 1]) * qs, -448.0f), 448.0f);
+      const float a3 = fminf(fmaxf(bf16hi_to_f(w[2 * h + 1]) * qs, -448.0f), 448.0f);
+      o[2 * j + h] = cvt_e4m3x2(a0, a1) | (cvt_e4m3x2(a2, a3) << 16);
+    }
+  }
+  st_stream_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
+  st_stream_v4(dst + 16, make_uint4(o[4], o[5], o[6], o[7]));
+}
+
+// The same for a block of a row without an E8M0 byte of 255: its values
+// e2m1 * f (f = 2^(e-127), exact in BF16) times qs round once either way, so
+// the block's factor f * qs (exact: f is a power of two; capped so that an
+// all-zero block far above the row's amax keeps its zeros) multiplies the
+// decoded codes directly, and every |v| <= 448 (1 + 2^-23) converts under the
+// saturating conversion exactly as clamp-then-convert does.
+__device__ __forceinline__ void quant_chunk32_fast(uint4 c, uint32_t e, float qs, uint8_t* dst) {
+  const float m = fminf(e8m0_to_f(e) * qs, 1e30f);
+  const uint32_t cw[4] = {c.x, c.y, c.z, c.w};
+  uint32_t o[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float v[8];
+    decode8_scaled(cw[j], m, v);
+    o[2 * j] = cvt_e4m3x4(v[0], v[1], v[2], v[3]);
+    o[2 * j + 1] = cvt_e4m3x4(v[4], v[5], v[6], v[7]);
+  }
+  st_stream_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
+  st_stream_v4(dst + 16, make_uint4(o[4], o[5], o[6], o[7]));
+}
+
+template <int kChunks>
 __global__ void __launch_bounds__(kRsThreads) dq_fp8_rowscale_kernel(
     const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales, int64_t M, int64_t Kb,
     float eps, uint8_t* __restrict__ out, float* __restrict__ scale_out) {
-  __shared__ uint32_t red_bits[kRsThreads / 32];
-  __shared__ float red_f[kRsThreads / 32];
+  __shared__ float red[kRsThreads / 32];
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int64_t nw = Kb / 4, S = Kb / 16;
-  constexpr int kHeld = kWords > 0 ? kWords : 1;
+  const int64_t nc = Kb / 16;  // 16-byte chunks (= blocks) per row
+  constexpr int kHeld = kChunks > 0 ? kChunks : 1;
   for (int64_t r = blockIdx.x; r < M; r += gridDim.x) {
     const uint8_t* cr = codes + r * Kb;
-    const uint8_t* sr = scales + r * S;
-    auto decode = [&](int64_t c) {
-      return dq_bf16_chunk(ld_stream_u32(cr + c * 4), (uint32_t)sr[c >> 2]);
-    };
-    uint4 v[kHeld];
-    uint32_t m = 0;
-    auto absmax4 = [&](const uint4& d) {
-      m = vmax_u16x2(m, d.x & 0x7FFF7FFFu);
-      m = vmax_u16x2(m, d.y & 0x7FFF7FFFu);
-      m = vmax_u16x2(m, d.z & 0x7FFF7FFFu);
-      m = vmax_u16x2(m, d.w & 0x7FFF7FFFu);
-    };
-    auto fmax4 = [](float a, const uint4& d) {
-      const uint32_t w[4] = {d.x, d.y, d.z, d.w};
+    const uint8_t* sr = scales + r * nc;
+    uint8_t* orow = out + r * 2 * Kb;
+    uint4 c[kHeld];
+    uint32_t e[kHeld];
+    float a = eps;
+    bool inf_scale = false;  // an E8M0 byte of 255: Inf and NaN values need the clamps
+    if constexpr (kChunks > 0) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        a = fmaxf(a, fabsf(bf16lo_to_f(w[j])));
-        a = fmaxf(a, fabsf(bf16hi_to_f(w[j])));
+      for (int i = 0; i < kChunks; ++i) {
+        const int64_t k = (int64_t)i * kRsThreads + t;
+        if (k < nc) {
+          c[i] = ld_stream_v4(cr + k * 16);
+          e[i] = ld_stream_u8(sr + k);
+        } else {
+          c[i] = make_uint4(0, 0, 0, 0);
+          e[i] = 0;
+        }
       }
-      return a;
-    };
-    if constexpr (kWords > 0) {
 #pragma unroll
-      for (int i = 0; i < kWords; ++i) {
-        const int64_t c = (int64_t)i * kRsThreads + t;
-        v[i] = c < nw ? decode(c) : make_uint4(0, 0, 0, 0);
-        absmax4(v[i]);
+      for (int i = 0; i < kChunks; ++i) {
+        a = fmaxf(a, block_amax(c[i], e[i]));
+        inf_scale = inf_scale || e[i] == 255u;
       }
     } else {
-      for (int64_t c = t; c < nw; c += kRsThreads) absmax4(decode(c));
-    }
-    uint32_t mb = max(m & 0xFFFFu, m >> 16);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-    if (lane == 0) red_bits[warp] = mb;
-    __syncthreads();
-    mb = max(max(red_bits[0], red_bits[1]), max(red_bits[2], red_bits[3]));
-    float amax;
-    if (mb <= 0x7F80u) {
-      amax = fmaxf(eps, __uint_as_float(mb << 16));
-    } else {  // a NaN is present: the float max ignores it
-      float a = eps;
-      if constexpr (kWords > 0) {
-#pragma unroll
-        for (int i = 0; i < kWords; ++i) a = fmax4(a, v[i]);
-      } else {
-        for (int64_t c = t; c < nw; c += kRsThreads) a = fmax4(a, decode(c));
+      for (int64_t k = t; k < nc; k += kRsThreads) {
+        a = fmaxf(a, block_amax(*reinterpret_cast<const uint4*>(cr + k * 16), sr[k]));
+        inf_scale = inf_scale || sr[k] == 255u;
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-      if (lane == 0) red_f[warp] = a;
-      __syncthreads();
-      amax = fmaxf(fmaxf(red_f[0], red_f[1]), fmaxf(red_f[2], red_f[3]));
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if (lane == 0) red[warp] = a;
+    inf_scale = __syncthreads_or(inf_scale);
+    const float amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();  // red is reused by the next row
     const float qs = 448.0f / amax;
     if (t == 0) scale_out[r] = amax / 448.0f;
-    auto quant8 = [&](int64_t c, const uint4& d) {
-      const uint32_t w[4] = {d.x, d.y, d.z, d.w};
-      uint32_t o[2];
+    if constexpr (kChunks > 0) {
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const float a0 = fminf(fmaxf(bf16lo_to_f(w[2 * j]) * qs, -448.0f), 448.0f);
-        const float a1 = fminf(fmaxf(bf16hi_to_f(w[2 * j]) * qs, -448.0f), 448.0f);
-        const float a2 = fminf(fmaxf(bf16lo_to_f(w[2 * j + 1]) * qs, -448.0f), 448.0f);
-        const float a3 = fminf(fmaxf(bf16hi_to_f(w[2 * j + 1]) * qs, -448.0f), 448.0f);
-        o[j] = cvt_e4m3x2(a0, a1) | (cvt_e4m3x2(a2, a3) << 16);
-      }
-      st_stream_v2(out + r * 2 * Kb + c * 8, make_uint2(o[0], o[1]));
-    };
-    if constexpr (kWords > 0) {
-#pragma unroll
-      for (int i = 0; i < kWords; ++i) {
-        const int64_t c = (int64_t)i * kRsThreads + t;
-        if (c < nw) quant8(c, v[i]);
+      for (int i = 0; i < kChunks; ++i) {
+        const int64_t k = (int64_t)i * kRsThreads + t;
+        if (k >= nc) continue;
+        if (inf_scale)
+          quant_chunk32(c[i], e[i], qs, orow + k * 32);
+        else
+          quant_chunk32_fast(c[i], e[i], qs, orow + k * 32);
       }
     } else {
-      for (int64_t c = t; c < nw; c += kRsThreads) quant8(c, decode(c));
+      for (int64_t k = t; k < nc; k += kRsThreads) {
+        if (inf_scale)
+          quant_chunk32(ld_stream_v4(cr + k * 16), ld_stream_u8(sr + k), qs, orow + k * 32);
+        else
+          quant_chunk32_fast(ld_stream_v4(cr + k * 16), ld_stream_u8(sr + k), qs, orow + k * 32);
+      }
     }
-    __syncthreads();  // red_* reused by the next row
   }
 }
 
@@ -285,11 +321,10 @@ static mxb_status mxfp4_to_fp8_rows(const void* input, const void* input_s, int6
   if (M == 0 || Kb == 0) return MXB_OK;
   MXB_REQUIRE(input && input_s && output_q && output_s, MXB_ERR_INVALID_ARGUMENT,
               "mxfp4_to_fp8: null pointer");
-  MXB_REQUIRE(aligned(input, 8) && aligned(input_s, 4) && aligned(output_q, 16) &&
-                  aligned(output_s, 4),
-              MXB_ERR_MISALIGNED, "mxfp4_to_fp8: misaligned pointer");
-  const int64_t lanes = M * Kb / 8;
-  const int grid = grid_for((const void*)dq_fp8_row_kernel<false>, lanes, kFp8RowUnroll);
+  MXB_REQUIRE(aligned(input, 16) && aligned(output_q, 16) && aligned(output_s, 4),
+              MXB_ERR_MISALIGNED, "mxfp4_to_fp8: input and output_q must be 16-byte aligned");
+  const int64_t lanes = M * Kb / 16;
+  const int grid = grid_for((const void*)dq_fp8_row_kernel<false>, lanes, kRowBlk);
   if (strict)
     dq_fp8_row_kernel<true><<<grid, 256, 0, to_cuda(stream)>>>(
         (const uint8_t*)input, (const uint8_t*)input_s, M, Kb, (uint8_t*)output_q,
@@ -322,21 +357,24 @@ extern "C" mxb_status mxb_per_token_Mxfp4ToFp8_rowscale(const void* input, const
   if (M == 0 || Kb == 0) return MXB_OK;
   MXB_REQUIRE(input && input_s && output_q && output_s, MXB_ERR_INVALID_ARGUMENT,
               "mxfp4_to_fp8_rowscale: null pointer");
-  MXB_REQUIRE(aligned(input, 4) && aligned(output_q, 8) && aligned(output_s, 4),
-              MXB_ERR_MISALIGNED, "mxfp4_to_fp8_rowscale: misaligned pointer");
-  const int64_t per = cdiv(Kb / 4, kRsThreads);
+  MXB_REQUIRE(aligned(input, 16) && aligned(output_q, 16) && aligned(output_s, 4),
+              MXB_ERR_MISALIGNED, "mxfp4_to_fp8_rowscale: input and output_q must be 16-byte "
+              "aligned");
+  const int64_t per = cdiv(Kb / 16, kRsThreads);
   const int grid = (int)(M < 148LL * 64 ? M : 148LL * 64);
   cudaStream_t s = to_cuda(stream);
   auto* ci = (const uint8_t*)input;
   auto* si = (const uint8_t*)input_s;
   auto* qo = (uint8_t*)output_q;
   auto* so = (float*)output_s;
-  if (per <= 4)
+  if (per <= 1)
+    dq_fp8_rowscale_kernel<1><<<grid, kRsThreads, 0, s>>>(ci, si, M, Kb, eps, qo, so);
+  else if (per <= 2)
+    dq_fp8_rowscale_kernel<2><<<grid, kRsThreads, 0, s>>>(ci, si, M, Kb, eps, qo, so);
+  else if (per <= 4)
     dq_fp8_rowscale_kernel<4><<<grid, kRsThreads, 0, s>>>(ci, si, M, Kb, eps, qo, so);
   else if (per <= 8)
     dq_fp8_rowscale_kernel<8><<<grid, kRsThreads, 0, s>>>(ci, si, M, Kb, eps, qo, so);
-  else if (per <= 16)
-    dq_fp8_rowscale_kernel<16><<<grid, kRsThreads, 0, s>>>(ci, si, M, Kb, eps, qo, so);
   else
     dq_fp8_rowscale_kernel<0><<<grid, kRsThreads, 0, s>>>(ci, si, M, Kb, eps, qo, so);
   return launch_status("mxfp4_to_fp8_rowscale");

@@ -20,6 +20,7 @@
 #include "capi_util.h"
 #include "common.cuh"
 #include "qrow.cuh"
+#include "tma.cuh"
 
 namespace mxb {
 namespace {
@@ -237,6 +238,73 @@ extern "C" mxb_status mxb_ep_combine(const void* recv, int64_t T, int64_t H, con
   return launch_status("ep_combine");
 }
 
+// The same permute with the SM's bulk-copy unit (16-byte aligned rows whose
+// scale part is a multiple of 16 bytes, e.g. H = 7168: 3584 + 224 bytes): a
+// one-warp CTA streams its rows through a ring of kPermStages shared-memory
+// slots.  A row arrives by two 1-D bulk loads (codes, scales) issued by lane
+// 0; lane k < topk reads destination k and issues that destination's two 1-D
+// bulk stores, so no register or load/store-unit traffic carries the bytes
+// and the destinations are stored in parallel.  A slot is refilled once every
+// lane's stores of the row it held have read it (bulk wait_group.read), one
+// row behind the current one.
+constexpr int kPermStages = 4;
+
+__global__ void __launch_bounds__(32) moe_permute_bulk_kernel(
+    const uint8_t* __restrict__ codes, int64_t cpitch, const uint8_t* __restrict__ scales,
+    int64_t spitch, int64_t rows, int64_t H, const int32_t* __restrict__ dst, int topk,
+    uint8_t* __restrict__ out_codes, uint8_t* __restrict__ out_scales, int64_t n_out,
+    uint32_t slot_bytes) {
+  extern __shared__ __align__(128) uint8_t psm[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(psm + kPermStages * slot_bytes);
+  const int lane = threadIdx.x;
+  const uint32_t cb = (uint32_t)(H / 2), sb = (uint32_t)(H / 32);
+  const int64_t first = blockIdx.x, step = gridDim.x;
+  const int64_t my = first < rows ? (rows - 1 - first) / step + 1 : 0;
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < kPermStages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  auto load = [&](int64_t j) {
+    const int s = (int)(j % kPermStages);
+    const int64_t i = first + j * step;
+    uint8_t* slot = psm + s * slot_bytes;
+    mbar_arrive_expect_tx(&full[s], cb + sb);
+    bulk_load_1d(slot, codes + i * cpitch, cb, &full[s]);
+    bulk_load_1d(slot + cb, scales + i * spitch, sb, &full[s]);
+  };
+  int64_t issued = my < kPermStages ? my : kPermStages;
+  if (lane == 0)
+    for (int64_t q = 0; q < issued; ++q) load(q);
+  int64_t j = 0;
+  for (; j < my; ++j) {
+    const int s = (int)(j % kPermStages);
+    const int64_t i = first + j * step;
+    const int32_t d = lane < topk ? dst[i * topk + lane] : -1;
+    const bool ok = mbar_wait(&full[s], (uint32_t)(j / kPermStages) & 1u);
+    if (!__all_sync(0xffffffffu, ok)) break;
+    const uint8_t* slot = psm + s * slot_bytes;
+    if (d >= 0 && d < n_out) {
+      bulk_store_1d(out_codes + (int64_t)d * cb, slot, cb);
+      bulk_store_1d(out_scales + (int64_t)d * sb, slot + cb, sb);
+    }
+    bulk_commit();
+    // refill the slot of row j-1 once every lane's stores have read it
+    if (j >= 1 && issued < my) {
+      bulk_wait_read_1();
+      __syncwarp();
+      if (lane == 0) load(issued);
+      ++issued;
+    }
+  }
+  // a row that never arrived: do not exit while requested copies may still land
+  if (lane == 0)
+    for (int64_t q = j; q < issued; ++q)
+      mbar_wait(&full[q % kPermStages], (uint32_t)(q / kPermStages) & 1u);
+  bulk_wait_all();
+}
+
 extern "C" mxb_status mxb_moe_permute_mxfp4(const void* codes, int64_t codes_pitch,
                                             const void* scales, int64_t scales_pitch, int64_t rows,
                                             int64_t H, const int32_t* dst, int topk,
@@ -253,6 +321,20 @@ extern "C" mxb_status mxb_moe_permute_mxfp4(const void* codes, int64_t codes_pit
                         reinterpret_cast<uintptr_t>(out_codes) |
                         reinterpret_cast<uintptr_t>(out_scales) | (uintptr_t)codes_pitch |
                         (uintptr_t)scales_pitch | (uintptr_t)(H / 2) | (uintptr_t)(H / 32);
+  const uint32_t slot = (uint32_t)((H / 2 + H / 32 + 127) / 128 * 128);
+  if ((any & 15) == 0 && (H / 32) % 16 == 0 && (size_t)slot * kPermStages <= 96 * 1024) {
+    const size_t smem = (size_t)slot * kPermStages + kPermStages * 8;
+    static const bool attr = cudaFuncSetAttribute((const void*)moe_permute_bulk_kernel,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  96 * 1024 + 64) == cudaSuccess;
+    MXB_REQUIRE(attr, MXB_ERR_CUDA, "moe_permute_mxfp4: cannot reserve shared memory");
+    const int per_sm = (int)max((size_t)1, min((size_t)32, (size_t)(200 * 1024) / (smem + 1024)));
+    const int g = (int)min((int64_t)148 * per_sm, rows);
+    moe_permute_bulk_kernel<<<g, 32, smem, to_cuda(stream)>>>(
+        (const uint8_t*)codes, codes_pitch, (const uint8_t*)scales, scales_pitch, rows, H, dst,
+        topk, (uint8_t*)out_codes, (uint8_t*)out_scales, n_out, slot);
+    return launch_status("moe_permute_mxfp4");
+  }
   const int64_t warps_needed = rows;
   const int grid = (int)min((int64_t)148 * 8, cdiv(warps_needed, kPermWarps));
   if ((any & 15) == 0)

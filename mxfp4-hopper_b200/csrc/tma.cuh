@@ -122,6 +122,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int32_t x, 
       "r"(x), "r"(y), "r"(smem_addr(src))
       : "memory");
 }
+// 1-D bulk copy of `bytes` contiguous bytes shared -> global (bulk group).
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_store_1d(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(dst)),
+               "r"(smem_addr(src)), "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

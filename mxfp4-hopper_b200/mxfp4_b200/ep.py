@@ -124,38 +124,109 @@ class Handle:
     recv_splits: list
 
 
-class MXFP4Dispatcher:
-    """Dispatch / combine over a process group (one rank per GPU)."""
+class EPError(RuntimeError):
+    """The expert-parallel exchange failed; the step's outputs are invalid."""
 
-    def __init__(self, group=None, num_experts: int = 256, hidden: int = 7168, kernels=None):
+
+class EPTimeout(EPError):
+    """A peer did not complete an exchange within the dispatcher's deadline
+    (late, hung, or gone)."""
+
+
+class EPProtocolError(EPError):
+    """A peer sent a count table that cannot be right (negative counts, or more
+    rows than it has tokens)."""
+
+
+class MXFP4Dispatcher:
+    """Dispatch / combine over a process group (one rank per GPU).
+
+    Failure detection (DeepEP's dispatch waits are bounded the same way,
+    deep_ep-1.2.1.diff:455-549): with `timeout_s`, every exchange is issued
+    asynchronously and waited for at most that long on the host; a peer that
+    is late, hung or gone raises EPTimeout (and a peer whose connection closed
+    raises EPError) instead of blocking the step forever, after which
+    `abort()` tears the process group down so that no collective stays queued.
+    The count table every rank receives is checked before any row moves:
+    counts must be non-negative and at most `max_tokens_per_rank`
+    (EPProtocolError otherwise)."""
+
+    def __init__(self, group=None, num_experts: int = 256, hidden: int = 7168, kernels=None,
+                 timeout_s: Optional[float] = None, max_tokens_per_rank: Optional[int] = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.num_experts = num_experts
         self.hidden = hidden
         self.k = kernels if kernels is not None else CudaKernels()
+        self.timeout_s = timeout_s
+        self.max_tokens_per_rank = max_tokens_per_rank
 
-    def _a2a(self, out, inp, out_splits, in_splits):
-        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+    def _wait(self, work, what: str):
+        if self.timeout_s is None:
+            work.wait()
+            return
+        import datetime
+        try:
+            ok = work.wait(timeout=datetime.timedelta(seconds=self.timeout_s))
+        except RuntimeError as e:  # the backends report a timeout or a lost peer this way
+            msg = str(e)
+            if "imed out" in msg or "imeout" in msg:
+                raise EPTimeout(f"rank {self.rank}: {what} not complete within "
+                                f"{self.timeout_s} s: {msg}") from e
+            raise EPError(f"rank {self.rank}: {what} failed: {msg}") from e
+        if ok is False:
+            raise EPTimeout(f"rank {self.rank}: {what} not complete within {self.timeout_s} s")
+
+    def _a2a(self, out, inp, out_splits, in_splits, what="all-to-all"):
+        if self.timeout_s is None:
+            dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+            return
+        w = dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group,
+                                   async_op=True)
+        self._wait(w, what)
+
+    def abort(self) -> None:
+        """Tears down the process group after a failed exchange (aborts the
+        NCCL communicator, so that no queued collective waits on a dead peer)."""
+        from torch.distributed import distributed_c10d as c10d
+        fn = getattr(c10d, "_abort_process_group", None)
+        if fn is not None:
+            fn(self.group)
+        else:  # older torch: destroying the group is the closest
+            dist.destroy_process_group(self.group)
+
+    def _check_counts(self, recv_counts: torch.Tensor) -> None:
+        c = recv_counts.tolist()
+        cap = self.max_tokens_per_rank
+        bad = [(src, n) for src, n in enumerate(c) if n < 0 or (cap is not None and n > cap)]
+        if bad:
+            raise EPProtocolError(f"rank {self.rank}: impossible row counts from "
+                                  f"(source, count) {bad} (limit {cap})")
 
     def dispatch(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor):
         """Returns (recv_wire [R, 17H/32] u8, recv_topk int32 [R, k] local ids,
         recv_w float32 [R, k], handle)."""
         route = build_route(topk_idx, topk_w, self.world, self.num_experts)
         recv_counts = torch.empty_like(route.send_counts)
-        dist.all_to_all_single(recv_counts, route.send_counts, group=self.group)
+        self._a2a(recv_counts, self._send_counts(route), None, None, "count exchange")
+        self._check_counts(recv_counts)
         send_splits = route.send_counts.tolist()
         recv_splits = recv_counts.tolist()
         S, R = sum(send_splits), sum(recv_splits)
         wire = self.k.pack(x, route.slots, S)
         recv_wire = torch.empty(R, wire.shape[1], dtype=torch.uint8, device=x.device)
-        self._a2a(recv_wire, wire, recv_splits, send_splits)
+        self._a2a(recv_wire, wire, recv_splits, send_splits, "row dispatch")
         kk = topk_idx.shape[1]
         recv_topk = torch.empty(R, kk, dtype=torch.int32, device=x.device)
         recv_w = torch.empty(R, kk, dtype=torch.float32, device=x.device)
-        self._a2a(recv_topk, route.local_topk, recv_splits, send_splits)
-        self._a2a(recv_w, route.local_w, recv_splits, send_splits)
+        self._a2a(recv_topk, route.local_topk, recv_splits, send_splits, "routing dispatch")
+        self._a2a(recv_w, route.local_w, recv_splits, send_splits, "weight dispatch")
         return recv_wire, recv_topk, recv_w, Handle(route, send_splits, recv_splits)
+
+    def _send_counts(self, route: Route) -> torch.Tensor:
+        """The count table row this rank sends (a hook for fault-injection tests)."""
+        return route.send_counts
 
     def identity_experts(self, recv_wire: torch.Tensor, recv_w: torch.Tensor) -> torch.Tensor:
         """Expert stage of the benchmark: every local expert is the identity, so
@@ -166,7 +237,7 @@ class MXFP4Dispatcher:
     def combine(self, y: torch.Tensor, handle: Handle) -> torch.Tensor:
         """Sends expert outputs back and sums each token's contributions."""
         back = torch.empty(sum(handle.send_splits), y.shape[1], dtype=y.dtype, device=y.device)
-        self._a2a(back, y, handle.send_splits, handle.recv_splits)
+        self._a2a(back, y, handle.send_splits, handle.recv_splits, "combine")
         return self.k.combine(back, handle.route.slots)
 
 
