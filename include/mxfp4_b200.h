@@ -323,6 +323,26 @@ mxb_status mxb_moe_permute_mxfp4(const void* codes, int64_t codes_pitch, const v
                                  int topk, void* out_codes, void* out_scales, int64_t n_out,
                                  mxb_stream_t stream);
 
+/* Transformer Engine's row_id_map for moe_permute with a mask routing map
+ * (the MXFP4 branch calls it at transformer_engine-2.8.diff:253-261,338-356;
+ * the map itself is upstream TE code the reference does not ship, restated
+ * here): routing_map bool (one byte) DEVICE [T, E]; the permuted output holds
+ * expert 0's tokens in token order, then expert 1's, ...; row_id_map int32
+ * DEVICE [T, 2E + 1]: per token its n destination rows (ascending expert
+ * order) in columns 0..n-1, those experts in columns E..E+n-1, n in column
+ * 2E, -1 elsewhere.  workspace: int32 DEVICE [E] (per-expert offsets). */
+mxb_status mxb_moe_make_row_id_map(const void* routing_map, int64_t T, int32_t E,
+                                   int32_t* row_id_map, int32_t* workspace, mxb_stream_t stream);
+
+/* mxb_moe_permute_mxfp4 driven by that row_id_map: token row t (codes and E8M0
+ * scales, any pitches as there) goes to rows row_id_map[t, 0..n-1] of
+ * out_codes [num_out_tokens, H/2] and out_scales [num_out_tokens, H/32]. */
+mxb_status mxb_moe_permute_mxfp4_row_id_map(const void* codes, int64_t codes_pitch,
+                                            const void* scales, int64_t scales_pitch, int64_t T,
+                                            int64_t H, const int32_t* row_id_map, int32_t E,
+                                            void* out_codes, void* out_scales,
+                                            int64_t num_out_tokens, mxb_stream_t stream);
+
 /* ---- fused dispatch / combine over NVLink peer memory ----
  * One buffer per rank with the layout below, mapped into every peer with CUDA
  * IPC (mxb_ipc_export / mxb_ipc_import); `bases` is a DEVICE array of the world

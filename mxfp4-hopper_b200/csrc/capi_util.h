@@ -4,6 +4,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -13,6 +15,15 @@
 namespace mxb {
 
 void set_error(const char* fmt, ...);
+
+// NVTX range over a host-side step (a C-ABI call, a pipeline chunk): shows in
+// Nsight Systems timelines; costs nothing when no tool is attached.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 inline cudaStream_t to_cuda(mxb_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -621,6 +621,7 @@ extern "C" mxb_status mxb_ipc_close(void* ptr, int64_t offset) {
 extern "C" mxb_status mxb_ep_p2p_counts(const uint64_t* bases, const mxb_ep_layout* L,
                                         const int32_t* send_counts, int parity, uint32_t epoch,
                                         mxb_stream_t stream) {
+  NvtxRange nvtx_range("mxb_ep_p2p_counts");
   mxb_status st = check_layout(L, "ep_p2p_counts");
   if (st != MXB_OK) return st;
   MXB_REQUIRE(bases && send_counts, MXB_ERR_INVALID_ARGUMENT, "ep_p2p_counts: null pointer");
@@ -632,6 +633,7 @@ extern "C" mxb_status mxb_ep_p2p_dispatch(const void* x, int64_t T, const int32_
                                           const int64_t* topk_idx, const float* topk_w,
                                           const uint64_t* bases, const mxb_ep_layout* L,
                                           int parity, mxb_stream_t stream) {
+  NvtxRange nvtx_range("mxb_ep_p2p_dispatch");
   mxb_status st = check_layout(L, "ep_p2p_dispatch");
   if (st != MXB_OK) return st;
   MXB_REQUIRE(T >= 0 && T <= L->tcap, MXB_ERR_INVALID_ARGUMENT,
@@ -648,6 +650,7 @@ extern "C" mxb_status mxb_ep_p2p_dispatch(const void* x, int64_t T, const int32_
 
 extern "C" mxb_status mxb_ep_p2p_barrier(const uint64_t* bases, const mxb_ep_layout* L,
                                          uint32_t epoch, mxb_stream_t stream) {
+  NvtxRange nvtx_range("mxb_ep_p2p_barrier");
   mxb_status st = check_layout(L, "ep_p2p_barrier");
   if (st != MXB_OK) return st;
   MXB_REQUIRE(bases, MXB_ERR_INVALID_ARGUMENT, "ep_p2p_barrier: null pointer");
@@ -657,6 +660,7 @@ extern "C" mxb_status mxb_ep_p2p_barrier(const uint64_t* bases, const mxb_ep_lay
 
 extern "C" mxb_status mxb_ep_p2p_return(const void* y, const uint64_t* bases,
                                         const mxb_ep_layout* L, int parity, mxb_stream_t stream) {
+  NvtxRange nvtx_range("mxb_ep_p2p_return");
   mxb_status st = check_layout(L, "ep_p2p_return");
   if (st != MXB_OK) return st;
   MXB_REQUIRE(bases, MXB_ERR_INVALID_ARGUMENT, "ep_p2p_return: null pointer");
@@ -669,6 +673,7 @@ extern "C" mxb_status mxb_ep_p2p_return(const void* y, const uint64_t* bases,
 extern "C" mxb_status mxb_ep_route(const int64_t* topk_idx, int64_t T, int32_t topk,
                                    int32_t experts_per_rank, int32_t world, int32_t* within,
                                    int32_t* send_counts, mxb_stream_t stream) {
+  NvtxRange nvtx_range("mxb_ep_route");
   MXB_REQUIRE(T >= 0 && topk >= 1 && topk <= 1024 && experts_per_rank >= 1 && world >= 1 &&
                   world <= 64,
               MXB_ERR_INVALID_ARGUMENT, "ep_route: bad arguments");
@@ -702,6 +707,7 @@ extern "C" mxb_status mxb_ep_route(const int64_t* topk_idx, int64_t T, int32_t t
 extern "C" mxb_status mxb_ep_p2p_combine(const void* back, int64_t T, int64_t H,
                                          const int32_t* within, const int32_t* send_counts,
                                          int32_t world, void* out, mxb_stream_t stream) {
+  NvtxRange nvtx_range("mxb_ep_p2p_combine");
   MXB_REQUIRE(T >= 0 && H > 0 && H % 8 == 0 && world >= 1 && world <= 64,
               MXB_ERR_INVALID_ARGUMENT, "ep_p2p_combine: bad arguments");
   if (T == 0) return MXB_OK;

@@ -95,6 +95,7 @@ extern "C" mxb_status mxb_quant_mxfp4_rowcol_host(const void* x_host, int64_t M,
               (long long)workspace_bytes, (long long)(kBufs * per));
   MXB_REQUIRE(aligned(workspace, 256), MXB_ERR_MISALIGNED,
               "quant_rowcol_host: workspace must be 256-byte aligned");
+  NvtxRange nvtx_call("mxb_quant_mxfp4_rowcol_host");
   int dev = 0;
   MXB_REQUIRE(cudaGetDevice(&dev) == cudaSuccess, MXB_ERR_CUDA, "quant_rowcol_host: no device");
   std::lock_guard<std::mutex> lk(g_mu);
@@ -120,6 +121,7 @@ extern "C" mxb_status mxb_quant_mxfp4_rowcol_host(const void* x_host, int64_t M,
   for (int64_t r0 = 0; r0 < M; r0 += R, ++i) {
     const int64_t rows = M - r0 < R ? M - r0 : R;
     const int b = i % kBufs;
+    NvtxRange nvtx_chunk("rowcol_host chunk");
     uint8_t* base = static_cast<uint8_t*>(workspace) + b * per;
     uint8_t* xd = base;
     uint8_t* crd = xd + up(R * K * 2);

@@ -47,6 +47,9 @@ SIGNATURES = {
     "mxb_ep_unpack": [_P, _I64, _I64, _P, _P, _P],
     "mxb_ep_combine": [_P, _I64, _I64, _P, _I, _P, _P],
     "mxb_moe_permute_mxfp4": [_P, _I64, _P, _I64, _I64, _I64, _P, _I, _P, _P, _I64, _P],
+    "mxb_moe_make_row_id_map": [_P, _I64, _I, _P, _P, _P],
+    "mxb_moe_permute_mxfp4_row_id_map": [_P, _I64, _P, _I64, _I64, _I64, _P, _I, _P, _P, _I64,
+                                         _P],
 }
 
 class EpLayout(ctypes.Structure):

@@ -72,6 +72,32 @@ class CudaKernels:
         return out
 
 
+def moe_permute_mxfp4(codes: torch.Tensor, scales: torch.Tensor, routing_map: torch.Tensor,
+                      num_out_tokens: Optional[int] = None):
+    """Transformer Engine's moe_permute (mask routing map) on the rowwise MXFP4
+    data of a token tensor (the branch at transformer_engine-2.8.diff:253-261,
+    338-356): codes uint8 [T, H/2] and E8M0 scales uint8 [T, H/32] (any row
+    pitch; wire rows too), routing_map bool [T, E].  Returns (out_codes
+    [num_out_tokens, H/2], out_scales [num_out_tokens, H/32], row_id_map int32
+    [T, 2E + 1]); expert 0's tokens come first, in token order."""
+    T, E = routing_map.shape
+    H = codes.shape[1] * 2
+    dev = codes.device
+    if num_out_tokens is None:
+        num_out_tokens = int(routing_map.sum().item())
+    rmap = routing_map.contiguous().view(torch.uint8)
+    rid = torch.empty(T, 2 * E + 1, dtype=torch.int32, device=dev)
+    ws = torch.empty(E, dtype=torch.int32, device=dev)
+    s = torch.cuda.current_stream(dev).cuda_stream
+    capi.call("mxb_moe_make_row_id_map", rmap.data_ptr(), T, E, rid.data_ptr(), ws.data_ptr(), s)
+    oc = torch.empty(num_out_tokens, H // 2, dtype=torch.uint8, device=dev)
+    os_ = torch.empty(num_out_tokens, H // 32, dtype=torch.uint8, device=dev)
+    capi.call("mxb_moe_permute_mxfp4_row_id_map", codes.data_ptr(), codes.stride(0),
+              scales.data_ptr(), scales.stride(0), T, H, rid.data_ptr(), E, oc.data_ptr(),
+              os_.data_ptr(), num_out_tokens, s)
+    return oc, os_, rid
+
+
 @dataclass
 class Route:
     """Where each token goes.  slots[t, g] is the row of the send buffer that

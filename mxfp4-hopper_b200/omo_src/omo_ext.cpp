@@ -8,11 +8,19 @@
 // There is no CPU path: a CPU tensor is an error.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <nvtx3/nvToolsExt.h>
 #include <torch/extension.h>
 
 #include "mxfp4_b200.h"
 
 namespace {
+
+// NVTX range over one operator call (visible in Nsight Systems timelines next
+// to the kernels it launches; costs nothing when no tool is attached).
+struct OmoRange {
+  explicit OmoRange(const char* name) { nvtxRangePushA(name); }
+  ~OmoRange() { nvtxRangePop(); }
+};
 
 #define OMO_CHECK_INPUT(x)                                               \
   TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor");               \
@@ -35,6 +43,7 @@ void check_dtype(const at::Tensor& t, at::ScalarType st, const char* name) {
 void omo_per_token_group_quant_fp4(at::Tensor input, at::Tensor output_q, at::Tensor output_s,
                                    int64_t group_size, double eps, double fp4_min, double fp4_max,
                                    bool scale_ue8m0) {
+  OmoRange nvtx_range("omo_per_token_group_quant_fp4");
   OMO_CHECK_INPUT(input);
   OMO_CHECK_INPUT(output_q);
   TORCH_CHECK(input.numel() % group_size == 0, "CHECK_EQ(input.numel() % group_size, 0) failed");
@@ -68,6 +77,7 @@ void omo_per_token_group_quant_fp4(at::Tensor input, at::Tensor output_q, at::Te
 void omo_per_token_Mxfp4ToBf16_dequant(at::Tensor input, at::Tensor input_s, at::Tensor output_q,
                                        at::Tensor output_s, int64_t group_size, double eps,
                                        double fp4_min, double fp4_max, bool scale_ue8m0) {
+  OmoRange nvtx_range("omo_per_token_Mxfp4ToBf16_dequant");
   (void)group_size; (void)eps; (void)fp4_min; (void)fp4_max;
   OMO_CHECK_INPUT(input);
   OMO_CHECK_INPUT(output_q);
@@ -119,6 +129,7 @@ void mxfp4_to_fp8_row_common(at::Tensor& input, at::Tensor& input_s, at::Tensor&
 void omo_per_token_Mxfp4ToFp8(at::Tensor input, at::Tensor input_s, at::Tensor output_q,
                               at::Tensor output_s, int64_t group_size, double eps, double fp4_min,
                               double fp4_max, bool scale_ue8m0) {
+  OmoRange nvtx_range("omo_per_token_Mxfp4ToFp8");
   (void)group_size; (void)eps; (void)fp4_min; (void)fp4_max;
   mxfp4_to_fp8_row_common(input, input_s, output_q, output_s, scale_ue8m0,
                           "omo_per_token_Mxfp4ToFp8");
@@ -129,6 +140,7 @@ void omo_per_token_Mxfp4ToFp8(at::Tensor input, at::Tensor input_s, at::Tensor o
 void omo_per_token_Mxfp4ToBf16ToFp8(at::Tensor input, at::Tensor input_s, at::Tensor output_q,
                                     at::Tensor output_s, int64_t group_size, double eps,
                                     double fp4_min, double fp4_max, bool scale_ue8m0) {
+  OmoRange nvtx_range("omo_per_token_Mxfp4ToBf16ToFp8");
   (void)group_size; (void)eps; (void)fp4_min; (void)fp4_max;
   mxfp4_to_fp8_row_common(input, input_s, output_q, output_s, scale_ue8m0,
                           "omo_per_token_Mxfp4ToBf16ToFp8");
@@ -142,6 +154,7 @@ void omo_per_token_group_quant_fp4_fused_ToFp8(at::Tensor input, at::Tensor outp
                                                at::Tensor output_bf16_s, int64_t group_size,
                                                double eps, double fp4_min, double fp4_max,
                                                bool scale_ue8m0) {
+  OmoRange nvtx_range("omo_per_token_group_quant_fp4_fused_ToFp8");
   // the checks of both halves (omo_per_token_group_quant_fp4 and omo_per_token_Mxfp4ToFp8)
   OMO_CHECK_INPUT(input);
   OMO_CHECK_INPUT(output_q);
@@ -176,6 +189,7 @@ void omo_per_token_group_quant_fp4_fused_ToFp8(at::Tensor input, at::Tensor outp
 void omo_per_token_Mxfp4ToFp8_col(at::Tensor input, at::Tensor input_s, at::Tensor output_q,
                                   at::Tensor output_s, int64_t group_size, double eps,
                                   double fp4_min, double fp4_max, bool scale_ue8m0) {
+  OmoRange nvtx_range("omo_per_token_Mxfp4ToFp8_col");
   (void)group_size; (void)eps; (void)fp4_min; (void)fp4_max;
   OMO_CHECK_INPUT(input);
   OMO_CHECK_INPUT(output_q);
@@ -205,6 +219,7 @@ void omo_per_token_Mxfp4ToFp8_col(at::Tensor input, at::Tensor input_s, at::Tens
 // ---- per_token_Mxfp4RowToBf16ToFp8Col.cu:204-247 (same shape checks)
 void omo_per_token_Mxfp4RowToBf16ToFp8Col(at::Tensor input, at::Tensor input_s,
                                           at::Tensor output_q, at::Tensor output_s, double eps) {
+  OmoRange nvtx_range("omo_per_token_Mxfp4RowToBf16ToFp8Col");
   OMO_CHECK_INPUT(input);
   OMO_CHECK_INPUT(output_q);
   TORCH_CHECK(input.dim() == 2, "CHECK_EQ(input.dim(), 2) failed");
@@ -236,6 +251,7 @@ void omo_per_token_Mxfp4RowToBf16ToFp8Col_msplit(at::Tensor input, at::Tensor in
                                                  at::Tensor m_splits, at::Tensor split_offsets,
                                                  at::Tensor scale_offsets, int64_t max_split_len,
                                                  double eps) {
+  OmoRange nvtx_range("omo_per_token_Mxfp4RowToBf16ToFp8Col_msplit");
   OMO_CHECK_INPUT(input);
   OMO_CHECK_INPUT(output_q);
   OMO_CHECK_INPUT(m_splits);
@@ -272,6 +288,7 @@ void omo_quant_mxfp4_rowcol(at::Tensor input, at::Tensor codes_row, at::Tensor s
                             at::Tensor codes_col, at::Tensor scales_col,
                             c10::optional<at::Tensor> scales_row_swizzled, double eps,
                             double fp4_min, double fp4_max) {
+  OmoRange nvtx_range("omo_quant_mxfp4_rowcol");
   OMO_CHECK_INPUT(input);
   check_dtype(input, at::kBFloat16, "input");
   TORCH_CHECK(input.dim() == 2, "input must be 2-D");
@@ -305,6 +322,7 @@ void omo_quant_mxfp4_rowcol(at::Tensor input, at::Tensor codes_row, at::Tensor s
 }
 
 void omo_swizzle_scales(at::Tensor scales, at::Tensor out) {
+  OmoRange nvtx_range("omo_swizzle_scales");
   OMO_CHECK_INPUT(scales);
   OMO_CHECK_INPUT(out);
   TORCH_CHECK(scales.dim() == 2, "scales must be 2-D");
@@ -318,6 +336,7 @@ void omo_swizzle_scales(at::Tensor scales, at::Tensor out) {
 
 void omo_per_token_quant_fp8(at::Tensor input, at::Tensor output_q, at::Tensor output_s,
                              double eps) {
+  OmoRange nvtx_range("omo_per_token_quant_fp8");
   OMO_CHECK_INPUT(input);
   OMO_CHECK_INPUT(output_q);
   OMO_CHECK_INPUT(output_s);
@@ -334,6 +353,7 @@ void omo_per_token_quant_fp8(at::Tensor input, at::Tensor output_q, at::Tensor o
 }
 
 void omo_per_token_dequant_fp8(at::Tensor input_q, at::Tensor input_s, at::Tensor output) {
+  OmoRange nvtx_range("omo_per_token_dequant_fp8");
   OMO_CHECK_INPUT(input_q);
   OMO_CHECK_INPUT(input_s);
   OMO_CHECK_INPUT(output);
@@ -352,6 +372,7 @@ void omo_per_token_dequant_fp8(at::Tensor input_q, at::Tensor input_s, at::Tenso
 // ---- operators with no reference binding: the next rows of the path
 void omo_swiglu_quant_mxfp4(at::Tensor input, at::Tensor output, at::Tensor codes,
                             at::Tensor scales, double eps, double fp4_min, double fp4_max) {
+  OmoRange nvtx_range("omo_swiglu_quant_mxfp4");
   OMO_CHECK_INPUT(input);
   OMO_CHECK_INPUT(output);
   OMO_CHECK_INPUT(codes);
@@ -375,6 +396,7 @@ void omo_swiglu_quant_mxfp4(at::Tensor input, at::Tensor output, at::Tensor code
 
 void omo_moe_permute_mxfp4(at::Tensor codes, at::Tensor scales, at::Tensor dst,
                            at::Tensor out_codes, at::Tensor out_scales) {
+  OmoRange nvtx_range("omo_moe_permute_mxfp4");
   OMO_CHECK_INPUT(codes);
   OMO_CHECK_INPUT(scales);
   OMO_CHECK_INPUT(dst);
@@ -402,6 +424,7 @@ void omo_moe_permute_mxfp4(at::Tensor codes, at::Tensor scales, at::Tensor dst,
 
 void omo_gemm_mxfp4(at::Tensor a_codes, at::Tensor a_scales_swizzled, at::Tensor b_codes,
                     at::Tensor b_scales_swizzled, at::Tensor c) {
+  OmoRange nvtx_range("omo_gemm_mxfp4");
   OMO_CHECK_INPUT(a_codes);
   OMO_CHECK_INPUT(a_scales_swizzled);
   OMO_CHECK_INPUT(b_codes);

@@ -221,3 +221,54 @@ def test_p2p_wait_gives_up_and_reports(cuda):
         torch.cuda.synchronize()
         lib.mxb_ep_reset_wait_timeouts()
     assert lib.mxb_ep_wait_timeouts() == 0
+
+
+# ------------------------------------------------------------------ row_id_map permute
+def _row_id_map_ref(rmap):
+    """Restated Transformer Engine mask-map row_id_map: experts in order, tokens
+    in order within an expert; per token its destinations, experts and count."""
+    T, E = rmap.shape
+    counts = rmap.sum(0)
+    offs = np.concatenate([[0], np.cumsum(counts)[:-1]])
+    rank = np.cumsum(rmap, 0) - 1
+    rid = np.full((T, 2 * E + 1), -1, np.int32)
+    for t in range(T):
+        ex = np.nonzero(rmap[t])[0]
+        n = len(ex)
+        rid[t, :n] = offs[ex] + rank[t, ex]
+        rid[t, E:E + n] = ex
+        rid[t, 2 * E] = n
+    return rid
+
+
+@pytest.mark.parametrize("T,E,k,H,wire", [(4096, 32, 8, 7168, True), (300, 256, 8, 7168, False),
+                                          (77, 64, 40, 7168, False), (77, 64, 40, 128, True),
+                                          (1, 8, 8, 512, False), (5, 16, 0, 256, False)])
+def test_moe_permute_row_id_map(cuda, T, E, k, H, wire):
+    """TE's moe_permute on MXFP4 rows from a mask routing map: the row_id_map
+    the device builds, and the permuted codes and scales, against a numpy
+    restatement; more than 32 destinations per row, empty tokens included."""
+    from mxfp4_b200.ep import moe_permute_mxfp4
+    g = np.random.default_rng(T + E + k)
+    rmap = np.zeros((T, E), bool)
+    for t in range(T):
+        if k:
+            rmap[t, g.choice(E, size=min(k, E), replace=False)] = True
+    if T > 3:
+        rmap[2] = False                       # a token routed nowhere
+    codes = g.integers(0, 256, (T, H // 2), dtype=np.uint8)
+    scales = g.integers(100, 150, (T, H // 32), dtype=np.uint8)
+    if wire:
+        src = torch.from_numpy(np.concatenate([codes, scales], axis=1)).to(cuda)
+        c_d, s_d = src[:, :H // 2], src[:, H // 2:]
+    else:
+        c_d, s_d = torch.from_numpy(codes).to(cuda), torch.from_numpy(scales).to(cuda)
+    oc, os_, rid = moe_permute_mxfp4(c_d, s_d, torch.from_numpy(rmap).to(cuda))
+    torch.cuda.synchronize()
+    rid_ref = _row_id_map_ref(rmap.astype(np.int64))
+    np.testing.assert_array_equal(rid.cpu().numpy(), rid_ref)
+    n_out = int(rmap.sum())
+    order = np.concatenate([np.nonzero(rmap[:, e])[0] for e in range(E)]) if n_out else \
+        np.zeros(0, np.int64)
+    np.testing.assert_array_equal(oc.cpu().numpy(), codes[order])
+    np.testing.assert_array_equal(os_.cpu().numpy(), scales[order])
