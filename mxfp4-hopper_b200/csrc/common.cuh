@@ -228,6 +228,27 @@ __device__ __forceinline__ uint32_t cvt_e4m3x4(float a0, float a1, float b0, flo
 // E8M0 byte -> float via the reference's BF16 reinterpretation.
 __device__ __forceinline__ float e8m0_to_f(uint32_t e) { return __uint_as_float(e << 23); }
 
+// Four code bytes (eight E2M1 codes) times the E8M0 factor of their block ->
+// eight BF16 values (two per word, element 2i in the low half), exactly the
+// reference's dequantize (per_token_Mxfp4ToBf16_dequant.cu:129-156): one exact
+// BF16 multiply by 2^(e-127) for e in [2, 254], the float product rounded to
+// BF16 for e in {0, 1, 255} (zero, the smallest binade, Inf / NaN).
+__device__ __forceinline__ uint4 dq_bf16_chunk(uint32_t w, uint32_t e) {
+  uint32_t o[4];
+  e2m1x4_to_bf16x4(w, o[0], o[1]);
+  e2m1x4_to_bf16x4(w >> 16, o[2], o[3]);
+  if (e - 2u <= 252u) {  // e in [2, 254]: exact BF16 product
+    const uint32_t s2 = (e << 7) | (e << 23);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = mul_bf16x2(o[i], s2);
+  } else {
+    const float s = e8m0_to_f(e);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = cvt_bf16x2(bf16lo_to_f(o[i]) * s, bf16hi_to_f(o[i]) * s);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 __host__ __device__ __forceinline__ int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 }  // namespace mxb

@@ -30,21 +30,6 @@ namespace {
 // output bytes.  Four chunks per lane are in flight per iteration.
 constexpr int kDqUnroll = 4;
 
-__device__ __forceinline__ uint4 dq_bf16_chunk(uint32_t w, uint32_t e) {
-  uint32_t o[4];
-  e2m1x4_to_bf16x4(w, o[0], o[1]);
-  e2m1x4_to_bf16x4(w >> 16, o[2], o[3]);
-  if (e - 2u <= 252u) {  // e in [2, 254]: exact BF16 product
-    const uint32_t s2 = (e << 7) | (e << 23);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) o[i] = mul_bf16x2(o[i], s2);
-  } else {
-    const float s = e8m0_to_f(e);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) o[i] = cvt_bf16x2(bf16lo_to_f(o[i]) * s, bf16hi_to_f(o[i]) * s);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
-}
 
 __global__ void __launch_bounds__(256) dq_bf16_kernel(const uint8_t* __restrict__ codes,
                                                       const uint8_t* __restrict__ scales,
