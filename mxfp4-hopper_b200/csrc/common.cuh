@@ -140,6 +140,20 @@ __device__ __forceinline__ void mul2_f32(uint32_t a, uint32_t b, float s, float&
       : "r"(a), "r"(b), "f"(s));
 }
 
+// (a, b) * (sa, sb), one mul.rn.f32x2; free of register moves when (a, b) and
+// (sa, sb) already sit in register pairs (e.g. neighbouring outputs of one
+// decode8_scaled and neighbouring words of one vector load).
+__device__ __forceinline__ void mul2_f32_pairs(float a, float b, float sa, float sb, float& ra,
+                                               float& rb) {
+  asm("{\n .reg .b64 x, y;\n"
+      " mov.b64 x, {%2, %3};\n"
+      " mov.b64 y, {%4, %5};\n"
+      " mul.rn.f32x2 x, x, y;\n"
+      " mov.b64 {%0, %1}, x;\n}"
+      : "=f"(ra), "=f"(rb)
+      : "f"(a), "f"(b), "f"(sa), "f"(sb));
+}
+
 // ---------------------------------------------------------------- E2M1 decode
 // BF16 bit patterns of the eight E2M1 magnitudes {0,.5,1,1.5,2,3,4,6}, split
 // into byte tables so that `prmt` can look up four nibbles at once.

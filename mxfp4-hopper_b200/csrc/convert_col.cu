@@ -693,20 +693,26 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
       const uint2 cl = *reinterpret_cast<const uint2*>(col_clamp + wc * 8);
       const bool clamp = (cl.x | cl.y) != 0u;
       uint8_t* orow = otile + (wc * 8) * 128 + ((rg ^ wc) << 3);
+      // column pairs (2j, 2j + 1) of a row are neighbouring decode outputs, so
+      // each mul.rn.f32x2 takes them with the pair of column scales as is
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float q[8];
+      for (int j = 0; j < 4; ++j) {
+        float q[8][2];
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          mul2_f32(__float_as_uint(v[2 * m][c]), __float_as_uint(v[2 * m + 1][c]), qv[c], q[2 * m],
-                   q[2 * m + 1]);
-        }
+        for (int k = 0; k < 8; ++k)
+          mul2_f32_pairs(v[k][2 * j], v[k][2 * j + 1], qv[2 * j], qv[2 * j + 1], q[k][0], q[k][1]);
         if (clamp) {
 #pragma unroll
-          for (int m = 0; m < 8; ++m) q[m] = fminf(fmaxf(q[m], -448.0f), 448.0f);
+          for (int k = 0; k < 8; ++k) {
+            q[k][0] = fminf(fmaxf(q[k][0], -448.0f), 448.0f);
+            q[k][1] = fminf(fmaxf(q[k][1], -448.0f), 448.0f);
+          }
         }
-        *reinterpret_cast<uint2*>(orow + c * 128) =
-            make_uint2(cvt_e4m3x4(q[0], q[1], q[2], q[3]), cvt_e4m3x4(q[4], q[5], q[6], q[7]));
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          *reinterpret_cast<uint2*>(orow + (2 * j + h) * 128) =
+              make_uint2(cvt_e4m3x4(q[0][h], q[1][h], q[2][h], q[3][h]),
+                         cvt_e4m3x4(q[4][h], q[5][h], q[6][h], q[7][h]));
       }
     }
     // tile i+1's factors into the other buffer (last read in tile i-1's step
