@@ -475,6 +475,33 @@ def time_ep(dev, stream, world, rank, args):
     nccl = {"ms_per_step": round(ms, 4), "value": round(world * T / (ms * 1e-3), 1),
             "transport": "NCCL all_to_all_single (torch.distributed)"}
 
+    # the C-ABI dispatcher over its own NCCL communicator (grouped send/recv)
+    from mxfp4_b200.ep import NcclCDispatcher, weight_sums
+    ids = [NcclCDispatcher.unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(ids, src=0)
+    cd = NcclCDispatcher(world, rank, ids[0], tokens=T, hidden=H, topk=8, num_experts=256)
+
+    def cstep():
+        rw, _, rwt = cd.dispatch(x, idx, w)
+        return cd.combine(d.k.unpack(rw, H, weight_sums(rwt)))
+
+    for _ in range(3):
+        cstep()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    e0.record(stream)
+    for _ in range(n):
+        cstep()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    tc = torch.tensor([e0.elapsed_time(e1) / n], dtype=torch.float64, device=dev)
+    dist.all_reduce(tc, op=dist.ReduceOp.MAX)
+    nccl_capi = {"ms_per_step": round(float(tc.item()), 4),
+                 "value": round(world * T / (float(tc.item()) * 1e-3), 1),
+                 "transport": "mxb_ep_nccl_dispatch / _combine (C ABI, ncclSend/ncclRecv)"}
+    dist.barrier()
+    cd.close()
+
     # fused path: quantize + NVLink peer stores in one kernel, no host sync
     from mxfp4_b200 import capi
     from mxfp4_b200.ep import P2PDispatcher
@@ -530,7 +557,7 @@ def time_ep(dev, stream, world, rank, args):
             "unit": "tokens/s", "ms_per_step": round(ms2, 4), "tokens_per_rank": T, "hidden": H,
             "experts": 256, "topk": 8, "payload": "mxfp4 dispatch, bf16 combine",
             "transport": "fused quantize + NVLink peer stores (CUDA IPC), device barriers",
-            "wait_timeouts": timeouts, "nccl_baseline": nccl,
+            "wait_timeouts": timeouts, "nccl_baseline": nccl, "nccl_capi": nccl_capi,
             "phases_us": phases_us,
             "nvlink_roofline": {"bound": "nvlink", "bytes_per_gpu_direction": int(bt.item()),
                                 "peak_gbs": NVLINK_GBS, "peak_source": "nominal NVLink 5",

@@ -343,6 +343,52 @@ mxb_status mxb_moe_permute_mxfp4_row_id_map(const void* codes, int64_t codes_pit
                                             void* out_codes, void* out_scales,
                                             int64_t num_out_tokens, mxb_stream_t stream);
 
+/* ---- dispatch / combine over an NCCL communicator ----
+ * The DeepEP-style exchange of the reference's MXFP4 payload
+ * (deep_ep-1.2.1.diff:455-549, megatron-0.15.0rc7.diff:290-311) for a caller
+ * holding an ncclComm_t (one process per GPU).  NCCL is opened at run time
+ * (libnccl.so.2); these entry points return MXB_ERR_UNSUPPORTED without it.
+ * comm is an ncclComm_t passed as void*. */
+#define MXB_EP_MAX_WORLD 64
+/* Host record a dispatch fills and its combine reads. */
+typedef struct {
+  int64_t send_counts[MXB_EP_MAX_WORLD]; /* rows this rank sent to each rank */
+  int64_t recv_counts[MXB_EP_MAX_WORLD]; /* rows it received from each rank */
+  int64_t n_send, n_recv, tokens;
+  int32_t world, rank, hidden, topk;
+} mxb_ep_handle;
+/* A fresh 128-byte NCCL unique id (rank 0 makes it and shares it). */
+mxb_status mxb_nccl_unique_id(void* id128);
+/* ncclCommInitRank: *comm receives the communicator. */
+mxb_status mxb_nccl_comm_init(void** comm, int32_t world, int32_t rank, const void* id128);
+mxb_status mxb_nccl_comm_destroy(void* comm);
+/* DEVICE workspace bytes a dispatch / combine pair needs (256-byte aligned; it
+ * carries the send slots from the dispatch to its combine). */
+int64_t mxb_ep_nccl_workspace_bytes(int64_t T, int32_t H, int32_t topk, int32_t world);
+/* Tokens x bf16 [T, H] (H % 128 == 0) routed by topk_idx int64 / topk_w float
+ * [T, topk] (global expert ids, experts_per_rank consecutive experts per rank):
+ * each token is quantized once to its wire row codes[H/2] || E8M0[H/32] and
+ * sent once to every rank hosting one of its experts.  On return the receive
+ * buffers hold handle->n_recv rows grouped by source rank (token order within):
+ * recv_wire uint8 [recv_cap, 17H/32], recv_meta [recv_cap] records of topk
+ * int32 expert ids local to this rank (-1 for experts elsewhere) followed by
+ * topk float routing weights (0 elsewhere).  The call synchronises `stream`
+ * once, after the per-peer counts arrive (MXB_ERR_INVALID_ARGUMENT if more rows
+ * arrive than recv_cap); the row exchange itself is asynchronous. */
+mxb_status mxb_ep_nccl_dispatch(void* comm, int32_t world, int32_t rank, const void* x, int64_t T,
+                                int32_t H, const int64_t* topk_idx, const float* topk_w,
+                                int32_t topk, int32_t experts_per_rank, void* workspace,
+                                int64_t workspace_bytes, void* recv_wire, void* recv_meta,
+                                int64_t recv_cap, mxb_ep_handle* handle, mxb_stream_t stream);
+/* y bf16 [handle->n_recv, H]: the expert output of each received row, in
+ * receive order.  Sends each row back to its source rank and writes
+ * out[t] = bf16(sum over ranks, in rank order, of the rows returned for token t)
+ * (DeepEP's BF16 combine, deep_ep-1.2.1.diff:132-139); out bf16 [T, H].
+ * Asynchronous on `stream`; `workspace` is the dispatch's. */
+mxb_status mxb_ep_nccl_combine(void* comm, const mxb_ep_handle* handle, const void* y,
+                               void* workspace, int64_t workspace_bytes, void* out,
+                               mxb_stream_t stream);
+
 /* ---- fused dispatch / combine over NVLink peer memory ----
  * One buffer per rank with the layout below, mapped into every peer with CUDA
  * IPC (mxb_ipc_export / mxb_ipc_import); `bases` is a DEVICE array of the world

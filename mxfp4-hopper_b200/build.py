@@ -30,7 +30,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
               "--expt-relaxed-constexpr", f"-I{INC}", f"-I{CSRC}"] + ARCH
 CU_SOURCES = ["quantize.cu", "dequant.cu", "convert_col.cu", "fp8_token.cu", "ep.cu", "ep_p2p.cu",
-              "gemm_mxfp4.cu"]
+              "ep_nccl.cu", "gemm_mxfp4.cu"]
 CPP_SOURCES = ["capi_util.cpp", "host_pipeline.cpp"]
 
 
@@ -77,7 +77,7 @@ def build_lib(force: bool = False, jobs: int = 8, verbose: bool = False) -> Path
                 print(r.stderr, file=sys.stderr)
     if force or cmds or not LIB.exists():
         _run([_nvcc(), "-shared", "-o", str(LIB)] + [str(o) for o in objs] + ARCH +
-             ["-lcudart"])
+             ["-lcudart", "-ldl"])
     return LIB
 
 

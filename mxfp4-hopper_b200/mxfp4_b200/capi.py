@@ -79,6 +79,25 @@ SIGNATURES.update({
     "mxb_ep_set_wait_polls": [_U32],
 })
 
+class EpHandle(ctypes.Structure):
+    """mxb_ep_handle of include/mxfp4_b200.h."""
+    _fields_ = [("send_counts", ctypes.c_int64 * 64), ("recv_counts", ctypes.c_int64 * 64),
+                ("n_send", ctypes.c_int64), ("n_recv", ctypes.c_int64), ("tokens", ctypes.c_int64),
+                ("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("hidden", ctypes.c_int32),
+                ("topk", ctypes.c_int32)]
+
+
+_HP = ctypes.POINTER(EpHandle)
+_I32 = ctypes.c_int32
+SIGNATURES.update({
+    "mxb_nccl_unique_id": [_P],
+    "mxb_nccl_comm_init": [ctypes.POINTER(ctypes.c_void_p), _I32, _I32, _P],
+    "mxb_nccl_comm_destroy": [_P],
+    "mxb_ep_nccl_dispatch": [_P, _I32, _I32, _P, _I64, _I32, _P, _P, _I32, _I32, _P, _I64, _P, _P,
+                             _I64, _HP, _P],
+    "mxb_ep_nccl_combine": [_P, _HP, _P, _P, _I64, _P, _P],
+})
+
 STATUS = {0: "MXB_OK", 1: "MXB_ERR_INVALID_ARGUMENT", 2: "MXB_ERR_MISALIGNED", 3: "MXB_ERR_CUDA",
           4: "MXB_ERR_UNSUPPORTED"}
 
@@ -111,6 +130,8 @@ def load() -> ctypes.CDLL:
         L.mxb_ep_wait_timeouts.restype = ctypes.c_uint
         L.mxb_ep_reset_wait_timeouts.restype = ctypes.c_uint
         L.mxb_gemm_wait_timeouts.restype = ctypes.c_uint
+        L.mxb_ep_nccl_workspace_bytes.argtypes = [_I64, _I32, _I32, _I32]
+        L.mxb_ep_nccl_workspace_bytes.restype = ctypes.c_int64
         L.mxb_quant_mxfp4_rowcol_host_workspace.argtypes = [_I64, _I64, _I64]
         L.mxb_quant_mxfp4_rowcol_host_workspace.restype = ctypes.c_int64
         _lib = L

@@ -412,3 +412,71 @@ class P2PDispatcher:
 
 class PeerTimeout(RuntimeError):
     """A bounded cross-GPU wait of the fused dispatcher ran out."""
+
+
+class NcclCDispatcher:
+    """Dispatch / combine through the C ABI over an NCCL communicator of its own
+    (mxb_ep_nccl_dispatch / mxb_ep_nccl_combine): the path a C or C++ caller
+    holding an ncclComm_t uses, here driven from Python.  Same results as
+    MXFP4Dispatcher.  `nccl_id` is the 128-byte id of rank 0's
+    `NcclCDispatcher.unique_id()`, shared by any means (e.g. a store)."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        import ctypes
+        buf = (ctypes.c_char * 128)()
+        capi.call("mxb_nccl_unique_id", ctypes.cast(buf, ctypes.c_void_p))
+        return bytes(buf)
+
+    def __init__(self, world: int, rank: int, nccl_id: bytes, tokens: int, hidden: int = 7168,
+                 topk: int = 8, num_experts: int = 256):
+        import ctypes
+        self.world, self.rank, self.hidden, self.topk = world, rank, hidden, topk
+        self.tokens, self.num_experts = tokens, num_experts
+        idb = (ctypes.c_char * 128).from_buffer_copy(nccl_id)
+        self.comm = ctypes.c_void_p()
+        capi.call("mxb_nccl_comm_init", ctypes.byref(self.comm), world, rank,
+                  ctypes.cast(idb, ctypes.c_void_p))
+        dev = torch.device("cuda", torch.cuda.current_device())
+        nb = int(capi.load().mxb_ep_nccl_workspace_bytes(tokens, hidden, topk, world))
+        self.ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+        self.cap = world * tokens
+        self.recv_wire = torch.empty(self.cap, wire_row_bytes(hidden), dtype=torch.uint8, device=dev)
+        self.recv_meta = torch.empty(self.cap, 2 * topk, dtype=torch.int32, device=dev)
+        self.handle = capi.EpHandle()
+
+    def dispatch(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor):
+        """Returns (recv_wire [R, 17H/32], recv_topk int32 [R, k], recv_w float32 [R, k])."""
+        import ctypes
+        T = x.shape[0]
+        idx = topk_idx.to(torch.int64).contiguous()
+        w = topk_w.float().contiguous()
+        s = torch.cuda.current_stream(x.device).cuda_stream
+        capi.call("mxb_ep_nccl_dispatch", self.comm, self.world, self.rank, x.data_ptr(), T,
+                  self.hidden, idx.data_ptr(), w.data_ptr(), self.topk,
+                  self.num_experts // self.world, self.ws.data_ptr(), self.ws.numel(),
+                  self.recv_wire.data_ptr(), self.recv_meta.data_ptr(), self.cap,
+                  ctypes.byref(self.handle), s)
+        R = int(self.handle.n_recv)
+        meta = self.recv_meta[:R]
+        return (self.recv_wire[:R], meta[:, :self.topk],
+                meta[:, self.topk:].contiguous().view(torch.float32))
+
+    def combine(self, y: torch.Tensor) -> torch.Tensor:
+        import ctypes
+        T = int(self.handle.tokens)
+        out = torch.empty(T, self.hidden, dtype=torch.bfloat16, device=y.device)
+        capi.call("mxb_ep_nccl_combine", self.comm, ctypes.byref(self.handle),
+                  y.contiguous().data_ptr(), self.ws.data_ptr(), self.ws.numel(), out.data_ptr(),
+                  torch.cuda.current_stream(y.device).cuda_stream)
+        return out
+
+    def close(self):
+        if self.comm:
+            capi.status_of("mxb_nccl_comm_destroy", self.comm)
+            self.comm = ctypes_null()
+
+
+def ctypes_null():
+    import ctypes
+    return ctypes.c_void_p()

@@ -76,3 +76,18 @@ def test_noalloc_split_rejects_before_touching_scratch(args):
     st = capi.status_of("mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit_noalloc", *args)
     assert st in (1, 2), (st, capi.last_error())
     assert "CUDA" not in capi.last_error()
+
+
+def test_nccl_unique_id_and_dispatch_argument_checks():
+    """The NCCL entry points open libnccl at run time: a unique id needs no GPU;
+    a dispatch with an impossible world size is rejected before any NCCL or CUDA
+    call."""
+    import ctypes
+    from mxfp4_b200.ep import NcclCDispatcher
+    a, b = NcclCDispatcher.unique_id(), NcclCDispatcher.unique_id()
+    assert len(a) == 128 and a != b
+    h = capi.EpHandle()
+    st = capi.status_of("mxb_ep_nccl_dispatch", 1, 0, 0, 1, 4, 7168, 1, 1, 8, 32, 1, 1 << 20, 1, 1,
+                        16, ctypes.byref(h), None)
+    assert st == 1 and "bad arguments" in capi.last_error()
+    assert capi.load().mxb_ep_nccl_workspace_bytes(4096, 7168, 8, 8) > 4096 * 8 * 3808

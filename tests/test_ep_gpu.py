@@ -106,6 +106,22 @@ def _worker(rank, world, port, q):
         recv_wire, recv_topk, recv_w, h = d.dispatch(x.to(dev), idx.to(dev), w.to(dev))
         out = d.combine(d.identity_experts(recv_wire, recv_w), h)
         ok_nccl = np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), exp)
+        # the C-ABI dispatcher over an NCCL communicator of its own
+        from mxfp4_b200.ep import NcclCDispatcher, weight_sums
+        ids = [NcclCDispatcher.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
+        cd = NcclCDispatcher(world, rank, ids[0], tokens=512, hidden=7168, topk=8,
+                             num_experts=256)
+        ok_c = True
+        for it in range(2):
+            xs, ids_, ws = syn.config5(rank + 50 * it, world, tokens=512 - 32 * it, hidden=7168)
+            rw, rt, rwt = cd.dispatch(xs.to(dev), ids_.to(dev), ws.to(dev))
+            yc = d.k.unpack(rw, 7168, weight_sums(rwt))
+            oc = cd.combine(yc)
+            ec = expected_round(xs, ids_, ws, world, 256)
+            ok_c &= np.array_equal(oc.cpu().view(torch.int16).numpy().view(np.uint16), ec)
+            ok_c &= bool(((rt >= -1) & (rt < 256 // world)).all())
+        cd.close()
         p2p = P2PDispatcher(None, tcap=512, hidden=7168, topk=8, num_experts=256)
         ok_p2p = True
         for it in range(3):  # several steps: parity and epochs advance
@@ -117,7 +133,7 @@ def _worker(rank, world, port, q):
         ok_p2p &= capi.load().mxb_ep_wait_timeouts() == 0
         dist.barrier()
         p2p.close()
-        q.put((rank, bool(ok_nccl and ok_p2p) or f"nccl {ok_nccl} p2p {ok_p2p}"))
+        q.put((rank, bool(ok_nccl and ok_p2p and ok_c) or f"nccl {ok_nccl} p2p {ok_p2p} c-abi {ok_c}"))
         dist.destroy_process_group()
     except Exception as e:
         q.put((rank, repr(e)))
