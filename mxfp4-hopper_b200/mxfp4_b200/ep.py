@@ -472,11 +472,7 @@ class NcclCDispatcher:
         return out
 
     def close(self):
+        import ctypes
         if self.comm:
             capi.status_of("mxb_nccl_comm_destroy", self.comm)
-            self.comm = ctypes_null()
-
-
-def ctypes_null():
-    import ctypes
-    return ctypes.c_void_p()
+            self.comm = ctypes.c_void_p()
