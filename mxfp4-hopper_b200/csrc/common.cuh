@@ -70,6 +70,14 @@ __device__ __forceinline__ uint32_t vmax_u16x2(uint32_t a, uint32_t b) {
   asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
+// Per-byte unsigned maximum, built on the native 16-bit-lane max (the byte
+// form vmax4 is a video instruction that sm_100 emulates with a long sequence:
+// replacing it took the per-row FP8 converter from 111 to 79 us).
+__device__ __forceinline__ uint32_t max_u8x4(uint32_t a, uint32_t b) {
+  return vmax_u16x2(a & 0x00FF00FFu, b & 0x00FF00FFu) |
+         (vmax_u16x2((a >> 8) & 0x00FF00FFu, (b >> 8) & 0x00FF00FFu) << 8);
+}
+
 // Per-lane max(|a|, |b|) of two BF16 pairs; a NaN in either input yields the
 // canonical NaN 0x7FFF (whose magnitude sorts above Inf), so one instruction
 // both reduces magnitudes and flags non-finite inputs.  The result's sign bits

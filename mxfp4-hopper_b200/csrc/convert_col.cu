@@ -32,11 +32,6 @@ constexpr uint32_t kCodeTileBytes = 128 * 64;
 
 __device__ const Fp8Lut g_lut_col = make_fp8_lut(true);
 
-__device__ __forceinline__ uint32_t vmax_u8x4(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("vmax4.u32.u32.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(0u));
-  return r;
-}
 
 // Loads the tile with one TMA and waits (bounded).  Returns false, for every
 // thread of the CTA, if the copy never completed.
@@ -110,8 +105,8 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
     uint32_t m0 = sc.x, m1 = sc.y;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      m0 = vmax_u8x4(m0, __shfl_xor_sync(0xffffffffu, m0, o));
-      m1 = vmax_u8x4(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+      m0 = max_u8x4(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+      m1 = max_u8x4(m1, __shfl_xor_sync(0xffffffffu, m1, o));
     }
     if (lane == 0) {
       red[rb * 2] = m0;
@@ -119,8 +114,8 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
     }
   }
   if (!load_code_tile(ctile, bar, &tmap, (int32_t)cb0, (int32_t)row0, kColCodeBytes)) return;
-  const uint32_t mx0 = vmax_u8x4(vmax_u8x4(red[0], red[2]), vmax_u8x4(red[4], red[6]));
-  const uint32_t mx1 = vmax_u8x4(vmax_u8x4(red[1], red[3]), vmax_u8x4(red[5], red[7]));
+  const uint32_t mx0 = max_u8x4(max_u8x4(red[0], red[2]), max_u8x4(red[4], red[6]));
+  const uint32_t mx1 = max_u8x4(max_u8x4(red[1], red[3]), max_u8x4(red[5], red[7]));
   // lane-dependent byte selectors of the two transpose rounds
   const uint32_t sel1 = (lane & 2) ? 0x3276u : 0x5410u;
   const uint32_t sel2 = (lane & 1) ? 0x3715u : 0x6240u;
