@@ -130,7 +130,8 @@ def test_fp8_rows_strict_config3_slice(cuda, orc):
 
 
 # ------------------------------------------------------------ per-row FP8
-@pytest.mark.parametrize("M,Kb", [(1, 16), (7, 8192), (64, 3584), (33, 16384), (512, 8192)])
+@pytest.mark.parametrize("M,Kb", [(1, 16), (7, 8192), (64, 3584), (33, 16384), (512, 8192),
+                                  (5, 32784)])  # the last: rows too long for registers
 def test_fp8_rowscale(cuda, orc, M, Kb):
     c, s = syn.config3(M, Kb, seed=M + Kb)
     cn, sn = c.numpy().copy(), s.numpy().copy()
