@@ -65,11 +65,9 @@ __device__ __forceinline__ bool load_code_tile(uint8_t* tile, uint64_t* bar, con
 // XOR-swizzled by (element & 3) << 1: the four lanes that write four element
 // rows of the same 4-byte column, and the two half-warps, land in eight
 // different chunks (no bank conflicts), and the 8 lanes that read one element
-// row read a permutation of its chunks.  50 KB of shared memory per CTA: four
-// CTAs per SM.
+// row read a permutation of its chunks.
 constexpr int kColPitch = 128;                 // bytes per element row of the transposed tile
 constexpr uint32_t kColCodeBytes = 128 * 128;  // 16 KiB
-constexpr size_t kColSmem = 1024 + kColCodeBytes + 256 * kColPitch + 4 * 8 + 16;
 
 // 4x4 byte transpose across lanes 4m..4m+3: in, lane i holds row i's bytes for
 // elements 0..3; out, lane i holds element i's bytes for rows 0..3.
@@ -77,6 +75,13 @@ __device__ __forceinline__ uint32_t transpose4x4(uint32_t w, uint32_t sel1, uint
   const uint32_t t = prmt(w, __shfl_xor_sync(0xffffffffu, w, 2), sel1);
   return prmt(t, __shfl_xor_sync(0xffffffffu, t, 1), sel2);
 }
+
+// The tile's 256 output rows leave in two phases of 128 (each warp converts
+// two of its four 32-column blocks per phase) through a staging tile of 128
+// element rows, so a CTA needs ~34 KB of shared memory and six CTAs share an
+// SM (four with a whole-tile staging area: 120 -> 115 us), which hides more of
+// the load latency this kernel waits on.
+constexpr size_t kColSmem = 1024 + kColCodeBytes + 128 * kColPitch + 4 * 8 + 16;
 
 __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant__ CUtensorMap tmap,
                                                            const uint8_t* __restrict__ scales,
@@ -87,8 +92,8 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* ctile = smem;                                      // 128 x 128 B (128-byte swizzle)
-  uint8_t* tr = smem + kColCodeBytes;                         // [element][row] FP8
-  uint32_t* red = reinterpret_cast<uint32_t*>(tr + 256 * kColPitch);  // [4 row blocks][2 words]
+  uint8_t* tr = smem + kColCodeBytes;                         // [element][row] FP8, one phase
+  uint32_t* red = reinterpret_cast<uint32_t*>(tr + 128 * kColPitch);  // [4 row blocks][2 words]
   uint64_t* bar = reinterpret_cast<uint64_t*>(red + 8);
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int rb = warp >> 1, hh = warp & 1;  // 32-row block, 64-byte half of the tile
@@ -123,40 +128,44 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
   // column rb * 32 + (lane & ~3), chunk rb * 2 + lane / 16 swizzled by (lane & 3) << 1
   uint8_t* trl = tr + (lane & 3) * kColPitch +
                  ((((rb * 2 + (lane >> 4)) ^ ((lane & 3) << 1))) << 4) + ((lane >> 2) & 3) * 4;
-
-#pragma unroll
-  for (int cc = 0; cc < 4; ++cc) {
-    const int q = 4 * hh + cc;  // 32-column block (16 code bytes) of the tile
-    const uint4 v = *reinterpret_cast<const uint4*>(ctile + r * 128 + ((q ^ (r & 7)) << 4));
-    const uint32_t e = ((q < 4 ? sc.x : sc.y) >> (8 * (q & 3))) & 0xFFu;
-    const uint32_t d = (((q < 4 ? mx0 : mx1) >> (8 * (q & 3))) & 0xFFu) - e;
-    const uint2 tb = __ldg(reinterpret_cast<const uint2*>(g_lut_col.v[d]));
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-#pragma unroll
-      for (int hw = 0; hw < 2; ++hw) {
-        const uint32_t f4 = lut_lookup4_nosign(w[j] >> (16 * hw), tb.x, tb.y);
-        const int n = q * 32 + j * 8 + hw * 4;
-        *reinterpret_cast<uint32_t*>(trl + n * kColPitch) = transpose4x4(f4, sel1, sel2);
-      }
-    }
-  }
-  __syncthreads();
   // scales: [M/128, 2*Kb], each block scale repeated over its 32 columns
   {
     const int q = t >> 5;
     const uint32_t wa = ((((q < 4 ? mx0 : mx1) >> (8 * (q & 3))) & 0xFFu) - 6u) & 0xFFu;
     scales_out[(row0 / 128) * (2 * Kb) + 2 * cb0 + t] = __uint_as_float(wa << 23);
   }
-  // output rows n = 2*cb0 + 0..255: 128 FP8 bytes each at columns row0..row0+127
-  uint8_t* ob = out + 2 * cb0 * M + row0;
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int i = k * kThreads + t;
-    const int n = i >> 3, part = i & 7;
-    const uint4 o = *reinterpret_cast<const uint4*>(&tr[n * kColPitch + ((part ^ ((n & 3) << 1)) << 4)]);
-    st_stream_v4(ob + n * M + part * 16, o);
+  for (int p = 0; p < 2; ++p) {
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const int q = 4 * p + 2 * hh + cc;  // 32-column block of the tile
+      const uint4 v = *reinterpret_cast<const uint4*>(ctile + r * 128 + ((q ^ (r & 7)) << 4));
+      const uint32_t e = ((q < 4 ? sc.x : sc.y) >> (8 * (q & 3))) & 0xFFu;
+      const uint32_t d = (((q < 4 ? mx0 : mx1) >> (8 * (q & 3))) & 0xFFu) - e;
+      const uint2 tb = __ldg(reinterpret_cast<const uint2*>(g_lut_col.v[d]));
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int hw = 0; hw < 2; ++hw) {
+          const uint32_t f4 = lut_lookup4_nosign(w[j] >> (16 * hw), tb.x, tb.y);
+          const int n = (q - 4 * p) * 32 + j * 8 + hw * 4;  // element row within the phase
+          *reinterpret_cast<uint32_t*>(trl + n * kColPitch) = transpose4x4(f4, sel1, sel2);
+        }
+      }
+    }
+    __syncthreads();
+    // output rows 2*cb0 + 128p + 0..127: 128 FP8 bytes each at columns row0..row0+127
+    uint8_t* ob = out + (2 * cb0 + 128 * p) * M + row0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = k * kThreads + t;
+      const int n = i >> 3, part = i & 7;
+      const uint4 o =
+          *reinterpret_cast<const uint4*>(&tr[n * kColPitch + ((part ^ ((n & 3) << 1)) << 4)]);
+      st_stream_v4(ob + n * M + part * 16, o);
+    }
+    if (p == 0) __syncthreads();  // the staging tile is refilled by phase 1
   }
 }
 
@@ -873,9 +882,8 @@ extern "C" mxb_status mxb_per_token_Mxfp4ToFp8_col(const void* input, const void
                            (int)kColSmem) == cudaSuccess;
   MXB_REQUIRE(attr_ok, MXB_ERR_CUDA, "mxfp4_to_fp8_col: cannot reserve shared memory");
   const dim3 grid((unsigned)(M / 128), (unsigned)(Kb / 128));
-  fp8_col_kernel<<<grid, kThreads, kColSmem, to_cuda(stream)>>>(tmap, (const uint8_t*)input_s, M,
-                                                                Kb, (uint8_t*)output_q,
-                                                                (float*)output_s);
+  fp8_col_kernel<<<grid, kThreads, kColSmem, to_cuda(stream)>>>(
+      tmap, (const uint8_t*)input_s, M, Kb, (uint8_t*)output_q, (float*)output_s);
   return launch_status("mxfp4_to_fp8_col");
 }
 
