@@ -76,12 +76,17 @@ __device__ __forceinline__ uint32_t transpose4x4(uint32_t w, uint32_t sel1, uint
   return prmt(t, __shfl_xor_sync(0xffffffffu, t, 1), sel2);
 }
 
-// The tile's 256 output rows leave in two phases of 128 (each warp converts
-// two of its four 32-column blocks per phase) through a staging tile of 128
-// element rows, so a CTA needs ~34 KB of shared memory and six CTAs share an
-// SM (four with a whole-tile staging area: 120 -> 115 us), which hides more of
-// the load latency this kernel waits on.
-constexpr size_t kColSmem = 1024 + kColCodeBytes + 128 * kColPitch + 4 * 8 + 16;
+// The tile's 256 output rows leave in four phases of 64 (each warp converts
+// one of its four 32-column blocks per phase) through a staging tile of 64
+// element rows (~26 KB of shared memory per CTA).  Measured on config 3:
+// whole-tile staging (4 CTAs per SM): 120 us; two phases: 115 us; four phases:
+// 89 us with the compiler's 40 registers (6 CTAs per SM), but 117 us when held
+// to 32 registers for 8 CTAs per SM: the gain is the loads the compiler keeps
+// in flight within a phase, not the occupancy.
+constexpr int kColPhases = 4;                  // output phases per tile (2 or 4)
+static_assert(kColPhases == 2 || kColPhases == 4, "each warp converts whole 32-column blocks");
+constexpr int kColPhaseRows = 256 / kColPhases;  // output rows staged per phase
+constexpr size_t kColSmem = 1024 + kColCodeBytes + kColPhaseRows * kColPitch + 4 * 8 + 16;
 
 __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant__ CUtensorMap tmap,
                                                            const uint8_t* __restrict__ scales,
@@ -93,7 +98,7 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
                                              ~uintptr_t(1023));
   uint8_t* ctile = smem;                                      // 128 x 128 B (128-byte swizzle)
   uint8_t* tr = smem + kColCodeBytes;                         // [element][row] FP8, one phase
-  uint32_t* red = reinterpret_cast<uint32_t*>(tr + 128 * kColPitch);  // [4 row blocks][2 words]
+  uint32_t* red = reinterpret_cast<uint32_t*>(tr + kColPhaseRows * kColPitch);  // [4 row blocks][2 words]
   uint64_t* bar = reinterpret_cast<uint64_t*>(red + 8);
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int rb = warp >> 1, hh = warp & 1;  // 32-row block, 64-byte half of the tile
@@ -135,10 +140,11 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
     scales_out[(row0 / 128) * (2 * Kb) + 2 * cb0 + t] = __uint_as_float(wa << 23);
   }
 #pragma unroll
-  for (int p = 0; p < 2; ++p) {
+  for (int p = 0; p < kColPhases; ++p) {
+    constexpr int kQ = 8 / kColPhases;  // 32-column blocks per phase
 #pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {
-      const int q = 4 * p + 2 * hh + cc;  // 32-column block of the tile
+    for (int cc = 0; cc < kQ / 2; ++cc) {
+      const int q = kQ * p + (kQ / 2) * hh + cc;  // phase p covers blocks kQ*p .. kQ*p + kQ - 1
       const uint4 v = *reinterpret_cast<const uint4*>(ctile + r * 128 + ((q ^ (r & 7)) << 4));
       const uint32_t e = ((q < 4 ? sc.x : sc.y) >> (8 * (q & 3))) & 0xFFu;
       const uint32_t d = (((q < 4 ? mx0 : mx1) >> (8 * (q & 3))) & 0xFFu) - e;
@@ -149,23 +155,23 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
 #pragma unroll
         for (int hw = 0; hw < 2; ++hw) {
           const uint32_t f4 = lut_lookup4_nosign(w[j] >> (16 * hw), tb.x, tb.y);
-          const int n = (q - 4 * p) * 32 + j * 8 + hw * 4;  // element row within the phase
+          const int n = (q - kQ * p) * 32 + j * 8 + hw * 4;  // element row within the phase
           *reinterpret_cast<uint32_t*>(trl + n * kColPitch) = transpose4x4(f4, sel1, sel2);
         }
       }
     }
     __syncthreads();
-    // output rows 2*cb0 + 128p + 0..127: 128 FP8 bytes each at columns row0..row0+127
-    uint8_t* ob = out + (2 * cb0 + 128 * p) * M + row0;
+    // output rows 2*cb0 + kColPhaseRows * p + 0..: 128 FP8 bytes each at columns row0..row0+127
+    uint8_t* ob = out + (2 * cb0 + kColPhaseRows * p) * M + row0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < kColPhaseRows * 8 / kThreads; ++k) {
       const int i = k * kThreads + t;
       const int n = i >> 3, part = i & 7;
       const uint4 o =
           *reinterpret_cast<const uint4*>(&tr[n * kColPitch + ((part ^ ((n & 3) << 1)) << 4)]);
       st_stream_v4(ob + n * M + part * 16, o);
     }
-    if (p == 0) __syncthreads();  // the staging tile is refilled by phase 1
+    if (p + 1 < kColPhases) __syncthreads();  // the staging tile is refilled by the next phase
   }
 }
 
