@@ -131,13 +131,6 @@ __global__ void __launch_bounds__(kTokThreads) fp8_quant_rows_long_kernel(
   }
 }
 
-// E4M3 byte (in the low 8 bits) -> float, exact: the magnitude bits placed at
-// float bit 20 read as 2^-120 times the value (normal or subnormal alike).
-__device__ __forceinline__ float e4m3_to_f(uint32_t b) {
-  const float f = __uint_as_float(((b & 0x7Fu) << 20) | ((b & 0x80u) << 24));
-  return f * 0x1p120f;
-}
-
 // One lane: 8 FP8 bytes -> 16 bytes of BF16; a warp instruction reads 256
 // contiguous bytes and writes 512.
 __global__ void __launch_bounds__(256) fp8_dequant_rows_kernel(const uint8_t* __restrict__ q,
@@ -149,18 +142,23 @@ __global__ void __launch_bounds__(256) fp8_dequant_rows_kernel(const uint8_t* __
        c += (int64_t)gridDim.x * blockDim.x) {
     const uint2 v = ld_stream_v2(q + c * 8);
     const float s = scale[c / per_row];
-    const uint32_t w[2] = {v.x, v.y};
+    // E4M3 pairs decoded by the hardware to f16 pairs (exact, NaN kept), widened
+    // on the FMA pipe, scaled in f32 and rounded once to BF16 (a NaN becomes the
+    // canonical BF16 NaN, as on the scalar path)
     uint32_t o[4];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      float f[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint32_t b = (w[j] >> (8 * u)) & 0xFFu;
-        f[u] = (b & 0x7Fu) == 0x7Fu ? __uint_as_float(0x7FC00000u) : e4m3_to_f(b) * s;
-      }
-      o[2 * j] = cvt_bf16x2(f[0], f[1]);
-      o[2 * j + 1] = cvt_bf16x2(f[2], f[3]);
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t pair = (j < 2 ? v.x : v.y) >> (16 * (j & 1));
+      float f0, f1;
+      asm("{\n .reg .b16 p, lo, hi;\n .reg .b32 h;\n"
+          " cvt.u16.u32 p, %2;\n"
+          " cvt.rn.f16x2.e4m3x2 h, p;\n"
+          " mov.b32 {lo, hi}, h;\n"
+          " add.rn.f32.f16 %0, lo, 0f80000000;\n"
+          " add.rn.f32.f16 %1, hi, 0f80000000;\n}"
+          : "=f"(f0), "=f"(f1)
+          : "r"(pair));
+      o[j] = cvt_bf16x2(f0 * s, f1 * s);
     }
     st_stream_v4(out + c * 16, make_uint4(o[0], o[1], o[2], o[3]));
   }
