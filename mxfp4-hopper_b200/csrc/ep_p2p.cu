@@ -203,7 +203,10 @@ __global__ void __launch_bounds__(kP2PThreads) ep_dispatch_p2p_kernel(
       const int64_t r = dr[g];
       if (r < 0) continue;
       const int64_t e = topk_idx[t * L.topk + j];
-      const bool here = e / L.experts_per_rank == g;
+      // e / experts_per_rank == g (C division) without a 64-bit division
+      const int64_t lo = (int64_t)g * L.experts_per_rank;
+      const bool here = e >= 0 ? (e >= lo && e < lo + L.experts_per_rank)
+                               : (g == 0 && e > -(int64_t)L.experts_per_rank);
       int32_t* m = reinterpret_cast<int32_t*>(peer(bases, g) + L.meta_off) + r * 2 * L.topk;
       m[j] = here ? (int32_t)(e - (int64_t)g * L.experts_per_rank) : -1;
       m[L.topk + j] = __float_as_int(here ? topk_w[t * L.topk + j] : 0.0f);
