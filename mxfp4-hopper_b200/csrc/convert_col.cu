@@ -449,56 +449,59 @@ __device__ __forceinline__ uint4 blend16(uint4 c, uint4 o, int a) {
   return make_uint4(r[0], r[1], r[2], r[3]);
 }
 
-// Writes an output row segment of `len` bytes starting at `row`, for any
-// alignment of `row` (a segment of the split path starts at n * m_i); called
-// by the 8 lanes of a row group, lane p holding data chunk p (bytes 16p..16p+15)
-// in d, with prev = chunk (p-1) mod 8 from the neighbouring lane.  The segment
-// is written as the 16-byte aligned chunks of memory it covers: memory chunk m
-// holds data bytes 16m - a .. 16m - a + 15 (a = row % 16), the top a bytes of
-// data chunk m-1 followed by the low 16 - a bytes of chunk m, which lane m
-// builds with funnel shifts over the window of words (prev, d).  Lane 0's
-// window (chunk 7, chunk 0) serves both partial chunks: memory chunk 0 (data
-// bytes 0 .. 15 - a) and memory chunk 8 (data bytes 128 - a .. 127).  Memory
-// chunk 8 is memory chunk 0 of the next 128-row block: with carry_out it is
-// kept in *carry instead of stored, and with merge_in this block's chunk 0 is
-// completed from *carry and stored whole.  Other partial chunks are written
-// in naturally aligned pieces, so neighbouring segments' bytes are never
-// touched.
-__device__ __forceinline__ void store_row_chunk(uint8_t* row, int p, uint4 d, uint4 prev, int len,
-                                                bool merge_in, bool carry_out, uint4* carry) {
-  const uintptr_t A = reinterpret_cast<uintptr_t>(row);
-  const int a = (int)(A & 15);
-  uint8_t* base = row - a;  // 16-byte aligned
-  uint4 o = d;
-  if (a != 0) {
-    // out word i = bytes 16 - a + 4i .. + 3 of W = (prev, d): words W[qs + i],
-    // W[qs + i + 1] funnel-shifted by rs bytes, qs = (16 - a) / 4, rs = (16 - a) % 4
-    const int sft = 16 - a, qs = sft >> 2, rs = sft & 3;
-    const uint32_t W[8] = {prev.x, prev.y, prev.z, prev.w, d.x, d.y, d.z, d.w};
-    uint32_t X[5];
+// Output row segments of the split path start at n * m_i and are rarely 16-byte
+// aligned.  A row segment of `len` bytes starting at `row` (a = row % 16) is
+// written as the 16-byte aligned chunks of memory it covers: memory chunk m
+// holds data bytes 16m - a .. 16m - a + 15, i.e. the top a bytes of data chunk
+// m-1 followed by the low 16 - a bytes of data chunk m (shift_window).  Chunks
+// 1-7 (the body) are written by lane m of the row's eight lanes from its own
+// and its neighbour's data chunk; the two edge chunks, 0 and 8, by one thread
+// per row in a second pass (store_row_edges), so that their heavier code does
+// not run serialised beside the body lanes.  Memory chunk 8 is memory chunk 0
+// of the next 128-row block: with carry_out it is kept in carry[n] instead of
+// stored, and with merge_in this block's chunk 0 is completed from carry[n]
+// and stored whole.  Other partial chunks are written in naturally aligned
+// pieces, so neighbouring segments' bytes are never touched.
+__device__ __forceinline__ uint4 shift_window(uint4 prev, uint4 d, int a) {
+  if (a == 0) return d;
+  // out word i = bytes 16 - a + 4i .. + 3 of W = (prev, d): words W[qs + i],
+  // W[qs + i + 1] funnel-shifted by rs bytes, qs = (16 - a) / 4, rs = (16 - a) % 4
+  const int sft = 16 - a, qs = sft >> 2, rs = sft & 3;
+  const uint32_t W[8] = {prev.x, prev.y, prev.z, prev.w, d.x, d.y, d.z, d.w};
+  uint32_t X[5];
 #pragma unroll
-    for (int k = 0; k < 5; ++k) {
-      const uint32_t lo2 = (qs & 1) ? W[k + 1] : W[k];
-      const uint32_t hi2 = (qs & 1) ? W[k + 3] : W[k + 2];
-      X[k] = (qs & 2) ? hi2 : lo2;
-    }
-    o.x = __funnelshift_r(X[0], X[1], 8 * rs);
-    o.y = __funnelshift_r(X[1], X[2], 8 * rs);
-    o.z = __funnelshift_r(X[2], X[3], 8 * rs);
-    o.w = __funnelshift_r(X[3], X[4], 8 * rs);
+  for (int k = 0; k < 5; ++k) {
+    const uint32_t lo2 = (qs & 1) ? W[k + 1] : W[k];
+    const uint32_t hi2 = (qs & 1) ? W[k + 3] : W[k + 2];
+    X[k] = (qs & 2) ? hi2 : lo2;
   }
-  if (p != 0) {
-    // memory chunk p covers data bytes [16p - a, 16p - a + 16) clipped to [0, len)
-    const int hi = min(16, len + a - 16 * p);
-    if (hi == 16) {
-      st_stream_v4(base + 16 * p, o);
-    } else if (hi > 0) {
-      store_bytes16(base + 16 * p, o, 0, hi);
-    }
-    return;
+  return make_uint4(__funnelshift_r(X[0], X[1], 8 * rs), __funnelshift_r(X[1], X[2], 8 * rs),
+                    __funnelshift_r(X[2], X[3], 8 * rs), __funnelshift_r(X[3], X[4], 8 * rs));
+}
+
+// Body chunk p (1..7) of a row segment; d and prev are data chunks p and p-1.
+__device__ __forceinline__ void store_row_body(uint8_t* row, int p, uint4 d, uint4 prev, int len) {
+  const int a = (int)(reinterpret_cast<uintptr_t>(row) & 15);
+  uint8_t* base = row - a;  // 16-byte aligned
+  // memory chunk p covers data bytes [16p - a, 16p - a + 16) clipped to [0, len)
+  const int hi = min(16, len + a - 16 * p);
+  if (hi <= 0) return;
+  const uint4 o = shift_window(prev, d, a);
+  if (hi == 16) {
+    st_stream_v4(base + 16 * p, o);
+  } else {
+    store_bytes16(base + 16 * p, o, 0, hi);
   }
-  // lane 0: memory chunk 0, bytes [a, min(16, len + a)) of this block
-  {
+}
+
+// Edge chunks 0 and 8 of a row segment; c7 and c0 are data chunks 7 and 0.
+__device__ __forceinline__ void store_row_edges(uint8_t* row, uint4 c7, uint4 c0, int len,
+                                                bool merge_in, bool carry_out, uint4* carry) {
+  const int a = (int)(reinterpret_cast<uintptr_t>(row) & 15);
+  uint8_t* base = row - a;  // 16-byte aligned
+  // the low a bytes: data 128 - a .. 127 (chunk 8); the rest: data 0 .. 15 - a (chunk 0)
+  const uint4 o = shift_window(c7, c0, a);
+  {  // memory chunk 0: bytes [a, min(16, len + a)) of this block
     const int hi = min(16, len + a);
     const uint4 v = (merge_in && a != 0) ? blend16(*carry, o, a) : o;
     const int lo = (merge_in || a == 0) ? 0 : a;
@@ -761,9 +764,18 @@ __global__ void __launch_bounds__(kThreads) fp8_colT_kernel(const __grid_constan
                                         __shfl_sync(0xffffffffu, o.y, src & 31),
                                         __shfl_sync(0xffffffffu, o.z, src & 31),
                                         __shfl_sync(0xffffffffu, o.w, src & 31));
-          if (n < g.cols)
-            store_row_chunk(dst - p * 16 + k * stride, p, o, prev, g.rows, g.merge_in, g.carry_out,
-                            carry + n);
+          if (n < g.cols && p != 0) store_row_body(dst - p * 16 + k * stride, p, o, prev, g.rows);
+        }
+        // edge chunks: one thread per output row
+        if (t < g.cols) {
+          const int n = t;
+          auto chunk = [&](int q) {  // data chunk q of staged row n
+            uint4 c = *reinterpret_cast<const uint4*>(otile + n * 128 + ((q ^ ((n >> 4) & 7)) << 4));
+            if ((n >> 3) & 1) c = make_uint4(c.z, c.w, c.x, c.y);
+            return c;
+          };
+          store_row_edges(out + g.out_base + (g.col0 + n) * g.out_pitch, chunk(7), chunk(0),
+                          g.rows, g.merge_in, g.carry_out, carry + n);
         }
       }
     }
