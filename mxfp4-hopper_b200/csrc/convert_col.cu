@@ -28,28 +28,8 @@ namespace mxb {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr uint32_t kCodeTileBytes = 128 * 64;
 
 __device__ const Fp8Lut g_lut_col = make_fp8_lut(true);
-
-
-// Loads the tile with one TMA and waits (bounded).  Returns false, for every
-// thread of the CTA, if the copy never completed.
-__device__ __forceinline__ bool load_code_tile(uint8_t* tile, uint64_t* bar, const CUtensorMap* map,
-                                               int32_t x, int32_t y,
-                                               uint32_t bytes = kCodeTileBytes) {
-  if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(bar, bytes);
-    tma_load_2d(tile, map, x, y, bar);
-  }
-  const bool ok = mbar_wait(bar, 0);
-  return !__syncthreads_or(!ok);
-}
 
 // ------------------------------------------------------------------ col (C4)
 // Tile: 128 rows x 128 code bytes (256 elements).  Rows are read as 128-byte
@@ -109,6 +89,14 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
   const int64_t S = Kb / 16;
   const int r = rb * 32 + lane;
 
+  // the tile's copy goes out first, so that it lands while the scale loads
+  // and their reduction run
+  if (t == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(bar, kColCodeBytes);
+    tma_load_2d(ctile, &tmap, (int32_t)cb0, (int32_t)row0, bar);
+  }
   // this row's eight E8M0 bytes (one per 32-column block of the tile)
   const uint2 sc = ld_stream_v2(scales + (row0 + r) * S + cb0 / 16);
   if (hh == 0) {
@@ -123,7 +111,8 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
       red[rb * 2 + 1] = m1;
     }
   }
-  if (!load_code_tile(ctile, bar, &tmap, (int32_t)cb0, (int32_t)row0, kColCodeBytes)) return;
+  __syncthreads();  // the barrier's initialisation and red[] are visible
+  if (__syncthreads_or(!mbar_wait(bar, 0))) return;  // the copy never completed
   const uint32_t mx0 = max_u8x4(max_u8x4(red[0], red[2]), max_u8x4(red[4], red[6]));
   const uint32_t mx1 = max_u8x4(max_u8x4(red[1], red[3]), max_u8x4(red[5], red[7]));
   // lane-dependent byte selectors of the two transpose rounds
@@ -293,7 +282,7 @@ __device__ __forceinline__ bool colT_next(ColTWalk& w, const ColTWalk& step, int
 // segment (units past a segment's end are empty).  Partial chunks remain only
 // at unit ends.  Digits (z, ss, s) advance by the step's digits without
 // division, as in the tile walk.
-constexpr int kUnitTiles = 4;
+constexpr int kUnitTiles = 2;
 
 struct SplitWalk {
   int64_t z;
