@@ -39,6 +39,28 @@ __device__ __forceinline__ uint32_t ld_stream_u8(const void* p) {
   asm volatile("ld.global.nc.L1::no_allocate.u8 %0, [%1];" : "=r"(r) : "l"(p));
   return r;
 }
+// Loads of data that neighbouring tiles read again soon (a tile's few bytes
+// of a longer E8M0 row): kept in L2 with the evict-last priority, so that the
+// sector is still there when the tiles beside it arrive.
+__device__ __forceinline__ uint64_t l2_keep_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint32_t ld_keep_u32(const void* p, uint64_t pol) {
+  uint32_t r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.u32 %0, [%1], %2;"
+               : "=r"(r)
+               : "l"(p), "l"(pol));
+  return r;
+}
+__device__ __forceinline__ uint2 ld_keep_v2(const void* p, uint64_t pol) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.u32 {%0,%1}, [%2], %3;"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p), "l"(pol));
+  return r;
+}
 // Streaming (evict-first) stores for outputs that are not re-read.
 __device__ __forceinline__ void st_stream_v4(void* p, uint4 v) {
   asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),

@@ -98,7 +98,8 @@ __global__ void __launch_bounds__(kThreads) fp8_col_kernel(const __grid_constant
     tma_load_2d(ctile, &tmap, (int32_t)cb0, (int32_t)row0, bar);
   }
   // this row's eight E8M0 bytes (one per 32-column block of the tile)
-  const uint2 sc = ld_stream_v2(scales + (row0 + r) * S + cb0 / 16);
+  // (evict-last: the three column tiles beside this one read the same sector)
+  const uint2 sc = ld_keep_v2(scales + (row0 + r) * S + cb0 / 16, l2_keep_policy());
   if (hh == 0) {
     uint32_t m0 = sc.x, m1 = sc.y;
 #pragma unroll
@@ -353,7 +354,9 @@ __device__ __forceinline__ uint32_t colT_scale_word(const uint8_t* scales, int64
   if (r < g.rows) {
     const uint8_t* sp = scales + (g.row_start + r) * S + g.col0 / 32;
     if (g.cols == 128 && (reinterpret_cast<uintptr_t>(sp) & 3) == 0) {
-      sc = ld_stream_u32(sp);
+      // the seven other 128-column tiles of these rows that share the 32-byte
+      // sector read it again (evict-last keeps it in L2 until they do)
+      sc = ld_keep_u32(sp, l2_keep_policy());
     } else {
 #pragma unroll
       for (int q = 0; q < 4; ++q)
