@@ -358,6 +358,7 @@ __device__ __forceinline__ uint64_t route_mask(const int64_t* __restrict__ topk_
 constexpr int kRouteTile = 256;
 constexpr int kRouteThreads = 1024;
 constexpr int kRouteMaxEntries = 16384;  // tiles * G held in shared memory (64 KB)
+constexpr int kRouteUnroll = 8;          // 16-byte groups per thread in flight (prefix pass)
 
 __global__ void __launch_bounds__(kRouteTile) ep_route_tile_kernel(
     const int64_t* __restrict__ topk_idx, int64_t T, int k, int experts_per_rank, int G,
@@ -413,8 +414,35 @@ __global__ void __launch_bounds__(kRouteThreads) ep_route_prefix_kernel(
     send_counts[g] = acc;
   }
   __syncthreads();
+  // Rewrite as 16-byte groups of 4 entries, kRouteUnroll groups per thread in
+  // flight (a tile's 256 * G entries are a multiple of 4, so a group never
+  // straddles two tiles); the ragged end, or a within[] that is not 16-byte
+  // aligned, entry by entry.
   const uint32_t n = (uint32_t)(T * G), row_elems = (uint32_t)(kRouteTile * G);
-  for (uint32_t i = threadIdx.x; i < n; i += kRouteThreads) {
+  const uint32_t n4 = (reinterpret_cast<uintptr_t>(within) & 15) == 0 ? n / 4 : 0;
+  int4* w4 = reinterpret_cast<int4*>(within);
+  for (uint32_t j0 = threadIdx.x; j0 < n4; j0 += kRouteUnroll * kRouteThreads) {
+    int4 v[kRouteUnroll];
+#pragma unroll
+    for (int u = 0; u < kRouteUnroll; ++u) {
+      const uint32_t j = j0 + u * kRouteThreads;
+      if (j < n4) v[u] = w4[j];
+    }
+#pragma unroll
+    for (int u = 0; u < kRouteUnroll; ++u) {
+      const uint32_t j = j0 + u * kRouteThreads;
+      if (j < n4) {
+        const uint32_t i = 4 * j;
+        const int32_t* pq = pref + (i / row_elems) * G;
+        const uint32_t g0 = i % (uint32_t)G, g1 = g0 + 1 == (uint32_t)G ? 0 : g0 + 1,
+                       g2 = g1 + 1 == (uint32_t)G ? 0 : g1 + 1,
+                       g3 = g2 + 1 == (uint32_t)G ? 0 : g2 + 1;
+        w4[j] = make_int4(v[u].x >= 0 ? v[u].x + pq[g0] : -1, v[u].y >= 0 ? v[u].y + pq[g1] : -1,
+                          v[u].z >= 0 ? v[u].z + pq[g2] : -1, v[u].w >= 0 ? v[u].w + pq[g3] : -1);
+      }
+    }
+  }
+  for (uint32_t i = 4 * n4 + threadIdx.x; i < n; i += kRouteThreads) {
     const uint32_t q = i / row_elems, g = i % (uint32_t)G;
     const int32_t w = within[i];
     within[i] = w >= 0 ? w + pref[q * G + g] : -1;
