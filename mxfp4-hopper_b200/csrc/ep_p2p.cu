@@ -37,6 +37,7 @@ constexpr uint32_t kPeerSpins = 1u << 22;  // default polls of ~64 ns sleep each
 static __device__ uint32_t g_ep_wait_polls = kPeerSpins;
 constexpr int kP2PThreads = 256;
 constexpr int kMaxScaleBytes = 2048;  // H / 32 for H <= 65536
+constexpr int kMaxMetaInts = 512;     // 2 * world * topk for world * topk <= 256
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -144,6 +145,7 @@ __global__ void __launch_bounds__(kP2PThreads) ep_dispatch_p2p_kernel(
   __shared__ __align__(16) uint8_t scale_bytes[kP2PWarps][kMaxScaleBytes];
   __shared__ __align__(16) uint32_t stage[kP2PWarps][32 * kDispatchBatch];
   __shared__ int64_t dst_row[kP2PWarps][32];
+  __shared__ __align__(16) int32_t meta_rows[kP2PWarps][kMaxMetaInts];
   const int G = L.world, H = L.hidden, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t rb = H / 2 + H / 32;
   const int steps = H / 256;  // H is a multiple of 512
@@ -197,19 +199,35 @@ __global__ void __launch_bounds__(kP2PThreads) ep_dispatch_p2p_kernel(
       *reinterpret_cast<uint4*>(row + H / 2 + q * 16) =
           *reinterpret_cast<const uint4*>(sb + q * 16);
     }
-    // routing metadata: expert id local to the destination (or -1), weight (or 0)
+    // routing metadata, one row of 2 * topk words per destination: expert ids
+    // local to the destination (or -1), then weights (or 0).  Rows are built in
+    // shared memory and leave as 16-byte stores when 2 * topk is a multiple of
+    // 4 (word stores otherwise), so that NVLink carries few small writes.
+    const int mrow = 2 * L.topk;
+    int32_t* mr = meta_rows[warp];
     for (int i = lane; i < G * L.topk; i += 32) {
       const int g = i / L.topk, j = i - g * L.topk;
-      const int64_t r = dr[g];
-      if (r < 0) continue;
+      if (dr[g] < 0) continue;
       const int64_t e = topk_idx[t * L.topk + j];
       // e / experts_per_rank == g (C division) without a 64-bit division
       const int64_t lo = (int64_t)g * L.experts_per_rank;
       const bool here = e >= 0 ? (e >= lo && e < lo + L.experts_per_rank)
                                : (g == 0 && e > -(int64_t)L.experts_per_rank);
-      int32_t* m = reinterpret_cast<int32_t*>(peer(bases, g) + L.meta_off) + r * 2 * L.topk;
-      m[j] = here ? (int32_t)(e - (int64_t)g * L.experts_per_rank) : -1;
-      m[L.topk + j] = __float_as_int(here ? topk_w[t * L.topk + j] : 0.0f);
+      mr[g * mrow + j] = here ? (int32_t)(e - lo) : -1;
+      mr[g * mrow + L.topk + j] = __float_as_int(here ? topk_w[t * L.topk + j] : 0.0f);
+    }
+    __syncwarp();
+    const int wpp = (mrow & 3) == 0 ? 4 : 1;  // words per store
+    const int pieces = mrow / wpp;
+    for (int i = lane; i < G * pieces; i += 32) {
+      const int g = i / pieces, q = i - g * pieces;
+      const int64_t r = dr[g];
+      if (r < 0) continue;
+      int32_t* m = reinterpret_cast<int32_t*>(peer(bases, g) + L.meta_off) + r * mrow + q * wpp;
+      if (wpp == 4)
+        *reinterpret_cast<int4*>(m) = *reinterpret_cast<const int4*>(mr + g * mrow + q * 4);
+      else
+        *m = mr[g * mrow + q];
     }
     __syncwarp();
   }
