@@ -24,9 +24,10 @@
 //   * warps 2..5 read the accumulators with tcgen05.ld (warp w owns lane
 //     quadrant w % 4 = rows 32(w%4) .. +31), convert to BF16 into the idle
 //     pipeline stages (128-byte swizzled boxes of 128 rows x 64 columns) and
-//     the tile leaves as four TMA stores (direct 32-byte row-piece stores:
-//     269.9 -> 262.4 us at 8192 x 8192 x 7168, 238 -> 200 us at
-//     16384 x 7168 x 2048, bytes identical).
+//     the tile leaves as four TMA stores (against direct 32-byte row-piece
+//     stores from registers and 16-column accumulator loads: 266.5 -> 257.7
+//     us at 8192 x 8192 x 7168, 237.7 -> 192.3 us at 16384 x 7168 x 2048,
+//     bytes identical).
 // Descriptor formats follow the Blackwell UMMA descriptors (CUTLASS
 // cute/arch/mma_sm100_desc.hpp).  Every wait is bounded; a CTA whose wait gives
 // up records it, skips its stores and still releases its tensor memory.
@@ -114,13 +115,26 @@ __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint3
       ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
       : "memory");
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+// 64 consecutive accumulator columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
+      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63"
+      "}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+        "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+        "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]),
+        "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]),
+        "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]),
+        "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]),
+        "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]),
+        "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() {
@@ -241,21 +255,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_mxfp4_kernel(
     // the pipeline stages hold the bf16 tile from here on
     const bool live = ok && !*((volatile int*)failed);
     if (live) {
+      const int r = quad * 32 + lane;
+      // one 64-column accumulator load per box (one wait per 64 columns, not 16)
 #pragma unroll 1
-      for (int c0 = 0; c0 < kTileN; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem + kAccCol + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
+      for (int b = 0; b < kTileN / 64; ++b) {
+        uint32_t v[64];
+        tmem_ld64(tmem + kAccCol + ((uint32_t)(quad * 32) << 16) + (uint32_t)(64 * b), v);
         tmem_ld_wait();
-        uint32_t o[8];
+        uint8_t* bx = smem + b * kCBoxBytes + r * 128;
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          o[i] = cvt_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-        // columns c0 .. c0 + 15 = 16-byte chunks k, k + 1 of row r of box c0 / 64
-        const int r = quad * 32 + lane, k = (c0 & 63) >> 3;
-        uint8_t* bx = smem + (c0 >> 6) * kCBoxBytes + r * 128;
-        *reinterpret_cast<uint4*>(bx + ((k ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-        *reinterpret_cast<uint4*>(bx + (((k + 1) ^ (r & 7)) << 4)) =
-            make_uint4(o[4], o[5], o[6], o[7]);
+        for (int k = 0; k < 8; ++k) {  // 16-byte chunk k = columns 64b + 8k .. + 7
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o[i] = cvt_bf16x2(__uint_as_float(v[8 * k + 2 * i]),
+                              __uint_as_float(v[8 * k + 2 * i + 1]));
+          *reinterpret_cast<uint4*>(bx + ((k ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
       }
     } else if (lane == 0 && quad == 0) {
       atomicAdd(timeouts, 1u);
