@@ -37,7 +37,7 @@ ALG_BYTES_ROWCOL = M2 * K2 * 2 + 2 * (M2 * K2 // 2 + M2 * K2 // 32)  # 411,041,7
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the headline
 # kernel from one ncu capture (profiles/quant_rowcol_config2.md).
-NCU_TRAFFIC_ROWCOL = 268_590_592 + 109_284_864  # read + write inside the launch; the rest of the writes drain from L2 afterwards
+NCU_TRAFFIC_ROWCOL = 268_551_680 + 108_301_824  # read + write inside the launch; the rest of the writes drain from L2 afterwards
 
 
 def measured_peaks():
