@@ -91,3 +91,47 @@ def test_nccl_unique_id_and_dispatch_argument_checks():
                         16, ctypes.byref(h), None)
     assert st == 1 and "bad arguments" in capi.last_error()
     assert capi.load().mxb_ep_nccl_workspace_bytes(4096, 7168, 8, 8) > 4096 * 8 * 3808
+
+
+@pytest.mark.parametrize("name,args,status,needle", [
+    # GEMM tiles: M % 128, N % 256, K % 256; 16-byte aligned operands
+    ("mxb_gemm_mxfp4", (1, 1, 1, 1, 100, 256, 256, 1, None), 1, "M % 128"),
+    ("mxb_gemm_mxfp4", (1, 1, 1, 1, 128, 128, 256, 1, None), 1, "N % 256"),
+    ("mxb_gemm_mxfp4", (1, 1, 1, 1, 128, 256, 128, 1, None), 1, "K % 256"),
+    ("mxb_gemm_mxfp4", (17, 1, 1, 1, 128, 256, 256, 1, None), 2, "aligned"),
+    ("mxb_gemm_mxfp4", (None, 1, 1, 1, 128, 256, 256, 1, None), 1, "null"),
+    # split converter with caller-supplied offsets
+    ("mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit",
+     (1, 1, 256, 40, 1, 1, 1, 1, 1, 2, 256, 1e-10, None), 1, "N % 32"),
+    ("mxb_per_token_Mxfp4RowToBf16ToFp8Col_msplit",
+     (None, 1, 256, 64, 1, 1, 1, 1, 1, 2, 256, 1e-10, None), 1, "null"),
+    # SwiGLU + quantize: H % 32
+    ("mxb_swiglu_quant_mxfp4", (1, 4, 40, 1, 1, 1, 1e-10, -6.0, 6.0, None), 1, "H % 32"),
+    ("mxb_swiglu_quant_mxfp4", (None, 4, 64, 1, 1, 1, 1e-10, -6.0, 6.0, None), 1, "null"),
+    # fused Q-row + rowwise FP8: group size 32 only (as the reference), K % 128
+    ("mxb_per_token_group_quant_fp4_fused_ToFp8",
+     (1, 4, 64, 64, 1, 1, 1, 1, 16, 1e-10, -6.0, 6.0, 0, None), 4, "group_size"),
+    ("mxb_per_token_group_quant_fp4_fused_ToFp8",
+     (1, 4, 40, 40, 1, 1, 1, 1, 32, 1e-10, -6.0, 6.0, 0, None), 1, "K % 128"),
+    # scale rule must be 0 (reference) or 1 (OCP)
+    ("mxb_quantize_mxfp4", (1, 64, 64, 64, 1, 1, 1, 1, None, 7, None), 1, "scale rule"),
+    ("mxb_quantize_mxfp4", (1, 48, 64, 64, 1, 1, 1, 1, None, 0, None), 1, "M % 32"),
+    # the strict and aliased rowwise FP8 converters keep the 1x128 group rule
+    ("mxb_per_token_Mxfp4ToFp8_strict", (1, 1, 4, 96, 1, 1, None), 1, "Kb % 64"),
+    ("mxb_per_token_Mxfp4ToBf16ToFp8", (1, 1, 4, 96, 1, 1, None), 1, "Kb % 64"),
+    ("mxb_per_token_Mxfp4ToFp8_rowscale", (1, 1, 4, 24, 1, 1, 1e-10, None), 1, "Kb % 16"),
+    ("mxb_per_token_Mxfp4ToFp8_rowscale", (None, 1, 4, 64, 1, 1, 1e-10, None), 1, "null"),
+    ("mxb_swizzle_scales", (None, 4, 4, 1, None), 1, "null"),
+    # EP wire rows: H % 128, 1 <= G <= 64
+    ("mxb_ep_pack", (1, 4, 40, 1, 0, 1, 1e-10, None), 1, "H % 128"),
+    ("mxb_ep_unpack", (1, 4, 40, 1, 1, None), 1, "H % 128"),
+])
+def test_entry_point_contracts(name, args, status, needle):
+    """Every remaining entry point with a shape or pointer rule rejects an
+    out-of-contract call with its status and a message naming the rule, before
+    any CUDA call (this container has no GPU: a CUDA call would report
+    MXB_ERR_CUDA)."""
+    assert capi.status_of(name, *args) == status
+    msg = capi.last_error()
+    assert needle in msg, msg
+    assert "CUDA" not in msg
