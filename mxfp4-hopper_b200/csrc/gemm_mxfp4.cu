@@ -6,32 +6,38 @@
 // scales_row_swizzled (the tcgen05 block-scale layout: a 512-byte atom holds
 // the 4 scales of 128 rows, row r at (r % 32) * 16 + (r / 32) * 4).
 //
-// One CTA computes a 128 x 256 tile of C in one f32 accumulator in tensor
-// memory (128 lanes x 256 columns); the K loop walks 256-element steps
-// through a 4-stage shared-memory ring:
+// Persistent: one CTA per SM walks the 128 x 256 tiles of C (tile =
+// blockIdx.x + i * gridDim.x, N-tiles fastest), each in one f32 accumulator in
+// tensor memory (128 lanes x 256 columns); K walks 256-element steps through a
+// 3-stage shared-memory ring that runs on across tile boundaries:
 //   * warp 0 (one thread) lands each step's A tile (128 rows x 128 bytes), B
 //     tile (256 rows x 128 bytes) with TMA (128-byte swizzle) and the step's
 //     scale atoms (2 for A, 4 for B, 512 bytes each) with 1-D bulk copies,
-//     completing on full[s];
-//   * warp 1 (one thread) copies the scale atoms into the stage's own tensor
-//     memory columns with tcgen05.cp (32 rows x 16 bytes replicated to the four
-//     lane quadrants: 4 columns per atom; B's 128-row blocks of one K-atom sit
-//     in consecutive column groups), issues 4 tcgen05.mma.kind::mxf4.
-//     block_scale.block32 of 128 x 256 x 64 per step (the scale byte pair of a
-//     K-half is selected by the top two bits of the TMEM scale addresses) and
-//     commits them to empty[s], which frees the stage when they have run;
-//     after the last step it commits to acc_full;
-//   * warps 2..5 read the accumulators with tcgen05.ld (warp w owns lane
-//     quadrant w % 4 = rows 32(w%4) .. +31), convert to BF16 into the idle
-//     pipeline stages (128-byte swizzled boxes of 128 rows x 64 columns) and
-//     the tile leaves as four TMA stores (against direct 32-byte row-piece
-//     stores from registers and 16-column accumulator loads: 266.5 -> 257.7
-//     us at 8192 x 8192 x 7168, 237.7 -> 192.3 us at 16384 x 7168 x 2048,
-//     bytes identical).
+//     completing on full[s]; it streams the next tile's steps while the
+//     current tile's epilogue runs;
+//   * warp 1 (one thread) waits for acc_empty (the accumulator read out), copies
+//     the scale atoms into the stage's own tensor memory columns with
+//     tcgen05.cp (32 rows x 16 bytes replicated to the four lane quadrants: 4
+//     columns per atom; B's 128-row blocks of one K-atom sit in consecutive
+//     column groups), issues 4 tcgen05.mma.kind::mxf4.block_scale.block32 of
+//     128 x 256 x 64 per step (the scale byte pair of a K-half is selected by
+//     the top two bits of the TMEM scale addresses) and commits them to
+//     empty[s], which frees the stage when they have run; after a tile's last
+//     step it commits to acc_full;
+//   * warps 2..5 read the accumulator with tcgen05.ld, 64 columns per load
+//     (warp w owns lane quadrant w % 4 = rows 32(w%4) .. +31), arrive on
+//     acc_empty, convert to BF16 into a staging area of four 128-byte swizzled
+//     boxes of 128 rows x 64 columns, and the tile leaves as four TMA stores
+//     that drain while the next tile's MMAs run.
+// Measured against one CTA per tile with a 4-stage ring (same epilogue, bytes
+// identical): 257.5 -> 229.8 us at 8192 x 8192 x 7168, 191.7 -> 140.5 us at
+// 16384 x 7168 x 2048.
 // Descriptor formats follow the Blackwell UMMA descriptors (CUTLASS
 // cute/arch/mma_sm100_desc.hpp).  Every wait is bounded; a CTA whose wait gives
 // up records it, skips its stores and still releases its tensor memory.
 #include <cuda_bf16.h>
+
+#include <algorithm>
 
 #include "capi_util.h"
 #include "common.cuh"
@@ -42,7 +48,7 @@ namespace {
 
 constexpr int kGemmThreads = 192;                         // producer, MMA, 4 epilogue warps
 constexpr int kTileM = 128, kTileN = 256, kTileK = 256;   // elements
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr uint32_t kABytes = 128 * 128;                   // 128 rows x 128 code bytes
 constexpr uint32_t kBBytes = 256 * 128;
 constexpr uint32_t kSfaBytes = 2 * 512, kSfbBytes = 4 * 512;
@@ -51,11 +57,12 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCol = 0;                           // accumulators: columns 0..255
 constexpr uint32_t kSfCol = 256;                          // per stage: 8 SFA + 16 SFB columns
 constexpr uint32_t kSfColsPerStage = 24;
-constexpr size_t kGemmSmem = 1024 + kStages * kStageBytes + 256;
-// Epilogue staging of the bf16 tile in the idle pipeline stages: four boxes of
-// 128 rows x 64 columns (128-byte rows, TMA 128-byte swizzle).
+// Epilogue staging of the bf16 tile beside the ring: four boxes of 128 rows x
+// 64 columns (128-byte rows, TMA 128-byte swizzle).
 constexpr uint32_t kCBoxBytes = 128 * 128;
-static_assert(4 * kCBoxBytes <= kStages * kStageBytes, "the C tile fits in the stages");
+constexpr size_t kGemmSmem = 1024 + kStages * kStageBytes + 4 * kCBoxBytes + 256;
+static_assert(kGemmSmem <= 227 * 1024, "one CTA per SM");
+static_assert(kSfCol + kStages * kSfColsPerStage <= kTmemCols, "scale columns fit in TMEM");
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
   // K-major, 128-byte swizzle: 8-row atoms of 128-byte rows, SBO = 1024 B,
@@ -149,15 +156,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_mxfp4_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint8_t* cst = smem + kStages * kStageBytes;  // C staging: 4 boxes of 128 x 64 bf16
+  uint64_t* full = reinterpret_cast<uint64_t*>(cst + 4 * kCBoxBytes);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
   int* failed = reinterpret_cast<int*>(tmem_base_slot + 1);
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int64_t m0 = (int64_t)blockIdx.y * kTileM, n0 = (int64_t)blockIdx.x * kTileN;
   const int ksteps = (int)(K / kTileK);
   const int64_t sp4 = K / 128;  // scale atoms per 128-row block along K
+  const int ntn = (int)(N / kTileN);
+  const int tiles = ntn * (int)(M / kTileM);
+  const int my_tiles =
+      (int)blockIdx.x < tiles ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
   if (t == 0) {
 #pragma unroll
@@ -166,6 +178,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_mxfp4_kernel(
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 4);
     fence_mbar_init();
     *failed = 0;
   }
@@ -181,111 +194,130 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_mxfp4_kernel(
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
-      int issued = 0;
-      for (int ks = 0; ks < ksteps; ++ks) {
-        const int s = ks % kStages;
-        if (ks >= kStages && !mbar_wait(&empty[s], (uint32_t)((ks / kStages - 1) & 1))) {
-          atomicExch(failed, 1);
-          break;
+      int issued = 0;  // global K steps over this CTA's tiles
+      bool ok = true;
+      for (int i = 0; ok && i < my_tiles; ++i) {
+        const int tile = (int)blockIdx.x + i * (int)gridDim.x;
+        const int64_t m0 = (int64_t)(tile / ntn) * kTileM, n0 = (int64_t)(tile % ntn) * kTileN;
+        for (int ks = 0; ks < ksteps; ++ks) {
+          const int g = issued, s = g % kStages;
+          if (g >= kStages && !mbar_wait(&empty[s], (uint32_t)((g / kStages - 1) & 1))) {
+            atomicExch(failed, 1);
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * kStageBytes;
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          const int32_t kx = ks * (kTileK / 2);
+          tma_load_2d(st, &tmap_a, kx, (int32_t)m0, &full[s]);
+          tma_load_2d(st + kABytes, &tmap_b, kx, (int32_t)n0, &full[s]);
+          tma_load_2d(st + kABytes + kABytes, &tmap_b, kx, (int32_t)(n0 + 128), &full[s]);
+          uint8_t* ssf = st + kABytes + kBBytes;
+          bulk_load_1d(ssf, sfa + ((m0 / 128) * sp4 + ks * 2) * 512, kSfaBytes, &full[s]);
+          bulk_load_1d(ssf + kSfaBytes, sfb + ((n0 / 128) * sp4 + ks * 2) * 512, kSfaBytes,
+                       &full[s]);
+          bulk_load_1d(ssf + kSfaBytes + kSfaBytes, sfb + ((n0 / 128 + 1) * sp4 + ks * 2) * 512,
+                       kSfaBytes, &full[s]);
+          issued = g + 1;
         }
-        uint8_t* st = smem + s * kStageBytes;
-        mbar_arrive_expect_tx(&full[s], kStageBytes);
-        const int32_t kx = ks * (kTileK / 2);
-        tma_load_2d(st, &tmap_a, kx, (int32_t)m0, &full[s]);
-        tma_load_2d(st + kABytes, &tmap_b, kx, (int32_t)n0, &full[s]);
-        tma_load_2d(st + kABytes + kABytes, &tmap_b, kx, (int32_t)(n0 + 128), &full[s]);
-        uint8_t* ssf = st + kABytes + kBBytes;
-        bulk_load_1d(ssf, sfa + ((m0 / 128) * sp4 + ks * 2) * 512, kSfaBytes, &full[s]);
-        bulk_load_1d(ssf + kSfaBytes, sfb + ((n0 / 128) * sp4 + ks * 2) * 512, kSfaBytes,
-                     &full[s]);
-        bulk_load_1d(ssf + kSfaBytes + kSfaBytes, sfb + ((n0 / 128 + 1) * sp4 + ks * 2) * 512,
-                     kSfaBytes, &full[s]);
-        issued = ks + 1;
       }
       // do not leave while copies of this CTA are still landing
-      for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
-        mbar_wait(&full[i % kStages], (uint32_t)((i / kStages) & 1));
+      for (int g = issued > kStages ? issued - kStages : 0; g < issued; ++g)
+        mbar_wait(&full[g % kStages], (uint32_t)((g / kStages) & 1));
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       bool ok = true;
-      for (int ks = 0; ks < ksteps; ++ks) {
-        const int s = ks % kStages;
-        if (!mbar_wait(&full[s], (uint32_t)((ks / kStages) & 1))) {
+      int g = 0;
+      for (int i = 0; ok && i < my_tiles; ++i) {
+        // the epilogue has read tile i-1's accumulator out of tensor memory
+        if (i > 0 && !mbar_wait(acc_empty, (uint32_t)((i - 1) & 1))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint8_t* st = smem + s * kStageBytes;
-        const uint8_t* ssf = st + kABytes + kBBytes;
-        const uint32_t sfc = tmem + kSfCol + (uint32_t)(s * kSfColsPerStage);
-        // scale atoms -> TMEM: A atoms a = 0,1 at sfc + 4a; B (half h, atom a) at sfc + 8 + 8h + 4a
+        for (int ks = 0; ks < ksteps; ++ks, ++g) {
+          const int s = g % kStages;
+          if (!mbar_wait(&full[s], (uint32_t)((g / kStages) & 1))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* st = smem + s * kStageBytes;
+          const uint8_t* ssf = st + kABytes + kBBytes;
+          const uint32_t sfc = tmem + kSfCol + (uint32_t)(s * kSfColsPerStage);
 #pragma unroll
-        for (int a = 0; a < 2; ++a) tc_copy_sf(sfc + 4 * a, smem_desc_sf(ssf + a * 512));
-        // B atoms: 128-row block h of K-atom a at sfc + 8 + 8a + 4h (rows 128..255
-        // follow rows 0..127 in the next four columns)
+          for (int a = 0; a < 2; ++a) tc_copy_sf(sfc + 4 * a, smem_desc_sf(ssf + a * 512));
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+          for (int h = 0; h < 2; ++h)
 #pragma unroll
-          for (int a = 0; a < 2; ++a)
-            tc_copy_sf(sfc + 8 + 8 * a + 4 * h, smem_desc_sf(ssf + kSfaBytes + (2 * h + a) * 512));
-        const uint64_t da = smem_desc_sw128(st);
-        const uint64_t db = smem_desc_sw128(st + kABytes);
+            for (int a = 0; a < 2; ++a)
+              tc_copy_sf(sfc + 8 + 8 * a + 4 * h,
+                         smem_desc_sf(ssf + kSfaBytes + (2 * h + a) * 512));
+          const uint64_t da = smem_desc_sw128(st);
+          const uint64_t db = smem_desc_sw128(st + kABytes);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          // K-half j = elements 64j .. 64j+63: atom j/2, scale bytes 2(j%2), 2(j%2)+1
-          const uint32_t sf_id = (uint32_t)(j & 1) * 2u;
-          const uint32_t tsfa = (sfc + 4 * (j >> 1)) | (sf_id << 30);
-          const uint32_t tsfb = (sfc + 8 + 8 * (j >> 1)) | (sf_id << 30);
-          tc_mma(tmem + kAccCol, da + (uint64_t)(2 * j), db + (uint64_t)(2 * j),
-                 gemm_idesc(sf_id, sf_id), tsfa, tsfb, (ks > 0 || j > 0) ? 1u : 0u);
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t sf_id = (uint32_t)(j & 1) * 2u;
+            const uint32_t tsfa = (sfc + 4 * (j >> 1)) | (sf_id << 30);
+            const uint32_t tsfb = (sfc + 8 + 8 * (j >> 1)) | (sf_id << 30);
+            tc_mma(tmem + kAccCol, da + (uint64_t)(2 * j), db + (uint64_t)(2 * j),
+                   gemm_idesc(sf_id, sf_id), tsfa, tsfb, (ks > 0 || j > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
         }
-        tc_commit(&empty[s]);  // the stage is free once these MMAs have run
+        tc_commit(acc_full);  // tile i's MMAs have completed when this arrives
       }
       if (!ok) atomicExch(failed, 1);
-      tc_commit(acc_full);  // every MMA issued so far has completed when this arrives
     }
   } else {
     // ------------------------------------------------ epilogue warps 2..5
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may read
-    const bool ok = mbar_wait(acc_full, 0u);
-    tc_fence_after();
-    // every MMA has completed (so every stage's copy has landed and been read):
-    // the pipeline stages hold the bf16 tile from here on
-    const bool live = ok && !*((volatile int*)failed);
-    if (live) {
-      const int r = quad * 32 + lane;
-      // one 64-column accumulator load per box (one wait per 64 columns, not 16)
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    for (int i = 0; i < my_tiles; ++i) {
+      const bool ok = mbar_wait(acc_full, (uint32_t)(i & 1));
+      tc_fence_after();
+      const bool live = ok && !*((volatile int*)failed);
+      // tile i-1's stores have read the staging boxes; the four warps leave
+      // together if any of them saw a wait give up
+      if (warp == 2 && lane == 0) bulk_wait_read_all();
+      if (named_sync_or(1, 128, !live)) {
+        if (lane == 0 && quad == 0) atomicAdd(timeouts, 1u);
+        break;
+      }
 #pragma unroll 1
       for (int b = 0; b < kTileN / 64; ++b) {
         uint32_t v[64];
         tmem_ld64(tmem + kAccCol + ((uint32_t)(quad * 32) << 16) + (uint32_t)(64 * b), v);
         tmem_ld_wait();
-        uint8_t* bx = smem + b * kCBoxBytes + r * 128;
+        uint8_t* bx = cst + b * kCBoxBytes + r * 128;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {  // 16-byte chunk k = columns 64b + 8k .. + 7
+        for (int k = 0; k < 8; ++k) {
           uint32_t o[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            o[i] = cvt_bf16x2(__uint_as_float(v[8 * k + 2 * i]),
-                              __uint_as_float(v[8 * k + 2 * i + 1]));
+          for (int q = 0; q < 4; ++q)
+            o[q] = cvt_bf16x2(__uint_as_float(v[8 * k + 2 * q]),
+                              __uint_as_float(v[8 * k + 2 * q + 1]));
           *reinterpret_cast<uint4*>(bx + ((k ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
-    } else if (lane == 0 && quad == 0) {
-      atomicAdd(timeouts, 1u);
-    }
-    // the tile leaves as four TMA stores of 128 rows x 64 columns
-    fence_proxy_async_smem();
-    named_sync(1, 128);
-    if (warp == 2 && lane == 0 && live) {
+      // the accumulator is free for tile i+1's MMAs
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+      fence_proxy_async_smem();
+      named_sync(1, 128);
+      if (warp == 2 && lane == 0) {
+        const int tile = (int)blockIdx.x + i * (int)gridDim.x;
+        const int64_t m0 = (int64_t)(tile / ntn) * kTileM, n0 = (int64_t)(tile % ntn) * kTileN;
 #pragma unroll
-      for (int b = 0; b < kTileN / 64; ++b)
-        tma_store_2d(&tmap_c, (int32_t)(n0 + 64 * b), (int32_t)m0, smem + b * kCBoxBytes);
-      bulk_commit();
-      bulk_wait_all();
+        for (int b = 0; b < kTileN / 64; ++b)
+          tma_store_2d(&tmap_c, (int32_t)(n0 + 64 * b), (int32_t)m0, cst + b * kCBoxBytes);
+        bulk_commit();
+      }
     }
+    if (warp == 2 && lane == 0) bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -330,7 +362,11 @@ extern "C" mxb_status mxb_gemm_mxfp4(const void* a_codes, const void* a_scales_s
   unsigned int* timeouts = nullptr;
   MXB_REQUIRE(cudaGetSymbolAddress((void**)&timeouts, g_gemm_timeouts) == cudaSuccess, MXB_ERR_CUDA,
               "gemm_mxfp4: cannot find the timeout counter");
-  const dim3 grid((unsigned)(N / kTileN), (unsigned)(M / kTileM));
+  // persistent: one CTA per SM walks tiles blockIdx.x, + gridDim.x, ...
+  const int64_t tiles = (N / kTileN) * (M / kTileM);
+  MXB_REQUIRE(tiles <= INT32_MAX, MXB_ERR_INVALID_ARGUMENT, "gemm_mxfp4: too many tiles");
+  const int ctas = persistent_ctas((const void*)gemm_mxfp4_kernel, kGemmThreads, kGemmSmem);
+  const dim3 grid((unsigned)std::min<int64_t>(tiles, ctas));
   gemm_mxfp4_kernel<<<grid, kGemmThreads, kGemmSmem, to_cuda(stream)>>>(
       ta, tb, tc, (const uint8_t*)a_scales_swizzled, (const uint8_t*)b_scales_swizzled, M, N, K,
       timeouts);
